@@ -1,0 +1,331 @@
+// tcgen05 GEMM for the encoder projections: out = act(A . W^T + bias).
+//
+// Replaces the reference's addMM(bias, x, W^T) projections (DeBERTa.swift:60-92: the
+// fused QKV projection, attention output, FFN up with GELU, FFN down) and the
+// classifier's first Linear + ReLU (DeBERTa.swift:437).
+//
+// Design (one CTA per SM, persistent over output tiles of BM x BN):
+//   warp 0      TMA producer: A tile [128 x 64] and W tile [BN x 64] per K-block into a
+//               STAGES-deep ring of 128B-swizzled shared-memory buffers (full/empty mbarriers).
+//   warp 1      allocates 2*BN TMEM columns; lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
+//               into one of two TMEM accumulators and commits to the ring's empty barriers
+//               and, per tile, to the accumulator-full barrier.
+//   warps 2-9   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+32, two warps per lane quarter split the columns), add bias,
+//               apply GELU / ReLU, round to fp16, store 16-byte vectors; then release the
+//               accumulator so the MMA warp can start the tile after next.
+// Every mbarrier wait is bounded (ptx::mbar_wait); on a timeout the kernel flags the error
+// word, drains its in-flight TMA loads and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace gdc {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 320;
+
+template <int BN>
+struct GemmShape {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+template <int BN, int ACT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                   const __half* __restrict__ bias, __half* __restrict__ out, int M, int N, int K, long long ldo,
+                   int* err) {
+  using S = GemmShape<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + S::kStages * S::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_b + S::kStages * S::kBBytes);
+  uint64_t* empty = full + S::kStages;
+  uint64_t* tfull = empty + S::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + kBM - 1) / kBM;
+  const int num_tiles = num_m * (N / BN);
+  const int kblocks = K / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::kStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&tfull[a], 1);
+      ptx::mbar_init(&tempty[a], 8);
+    }
+    ptx::mbar_init(drain, 1);
+    ptx::fence_barrier_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, S::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      ptx::prefetch_tensor_map(&tm_a);
+      ptx::prefetch_tensor_map(&tm_w);
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mb = tile % num_m;
+        const int nb = tile / num_m;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1u, err)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          ptx::tma_load_2d(s_a + stage * S::kABytes, &tm_a, kb * kBK, mb * kBM, &full[stage]);
+          ptx::tma_load_2d(s_b + stage * S::kBBytes, &tm_w, kb * kBK, nb * BN, &full[stage]);
+          ++issued;
+          if (++stage == S::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: the last issue to each ring slot must have landed before the CTA exits.
+      const long long tail = issued < S::kStages ? issued : S::kStages;
+      for (long long j = 0; j < tail; ++j) {
+        // walk back from the most recent issue
+        int s = stage - 1 - int(j);
+        uint32_t ph = phase;
+        while (s < 0) {
+          s += S::kStages;
+          ph ^= 1u;
+        }
+        if (!ptx::mbar_try_wait(&full[s], ph)) {
+          const unsigned long long t0 = ptx::globaltimer();
+          while (!ptx::mbar_try_wait(&full[s], ph) && ptx::globaltimer() - t0 < ptx::kTimeoutNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::idesc_f16_f32(kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!ptx::mbar_wait(&tempty[acc], aphase ^ 1u, err)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!ptx::mbar_wait(&full[stage], phase, err)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a_addr = ptx::smem_u32(s_a + stage * S::kABytes);
+          const uint32_t b_addr = ptx::smem_u32(s_b + stage * S::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            ptx::umma_f16_ss(d_tmem, ptx::desc_kmajor_sw128(a_addr + k * 32), ptx::desc_kmajor_sw128(b_addr + k * 32),
+                             idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          ptx::umma_commit(&empty[stage]);
+          if (++stage == S::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        ptx::umma_commit(&tfull[acc]);
+      }
+      // Drain all issued MMAs before TMEM is released.
+      ptx::umma_commit(drain);
+      if (!ptx::mbar_try_wait(drain, 0)) {
+        const unsigned long long t0 = ptx::globaltimer();
+        while (!ptx::mbar_try_wait(drain, 0) && ptx::globaltimer() - t0 < ptx::kTimeoutNs) {
+        }
+      }
+    }
+  } else {
+    // Epilogue warps 2..9.
+    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    const int col_half = (warp - 2) >> 2;   // which half of the BN columns
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      if (!ptx::mbar_wait(&tfull[acc], aphase, err)) break;
+      ptx::tc_fence_after();
+      const int mb = tile % num_m;
+      const int nb = tile / num_m;
+      const int row = mb * kBM + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 2; c += 32) {
+        const int col = col_half * (BN / 2) + c;
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(t_row + uint32_t(col), r);
+        ptx::tmem_wait_ld();
+        const int n0 = nb * BN + col;
+        const uint4* bsrc = reinterpret_cast<const uint4*>(bias + n0);
+        uint32_t packed[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 bv = __ldg(bsrc + q);
+          const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 bf = __half22float2(bh[j]);
+            float v0 = __uint_as_float(r[q * 8 + 2 * j]) + bf.x;
+            float v1 = __uint_as_float(r[q * 8 + 2 * j + 1]) + bf.y;
+            if (ACT == kActGelu) {
+              v0 = gelu_erf(v0);
+              v1 = gelu_erf(v1);
+            } else if (ACT == kActRelu) {
+              v0 = fmaxf(v0, 0.f);
+              v1 = fmaxf(v1, 0.f);
+            }
+            packed[q * 4 + j] = ptx::pack_half2(v0, v1);
+          }
+        }
+        if (row < M) {
+          uint4* dst = reinterpret_cast<uint4*>(out + (long long)row * ldo + n0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(packed[q * 4], packed[q * 4 + 1], packed[q * 4 + 2], packed[q * 4 + 3]);
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, S::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D fp16 tensor map: `rows` x `cols` (cols contiguous), row pitch `ld` elements,
+// box = box_rows x 64 columns, 128-byte swizzle, out-of-bounds rows read as zero.
+gdc_status make_tmap(CUtensorMap* map, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                     uint32_t box_rows) {
+  auto fn = get_encode_fn();
+  if (!fn) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * sizeof(__half)};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return GDC_OK;
+}
+
+template <int BN, int ACT>
+gdc_status launch_gemm_variant(const CUtensorMap& ta, const CUtensorMap& tw, const __half* bias, __half* out,
+                               long long ldo, int M, int N, int K, cudaStream_t stream, int* err) {
+  using S = GemmShape<BN>;
+  auto kern = gemm_tn_kernel<BN, ACT>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return set_error(GDC_ERR_CUDA, "device ordinal out of range");
+  if (!configured[dev]) {
+    GDC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes));
+    configured[dev] = true;
+  }
+  const int num_tiles = ((M + kBM - 1) / kBM) * (N / BN);
+  const int grid = num_tiles < device_sm_count(dev) ? num_tiles : device_sm_count(dev);
+  kern<<<grid, kThreads, S::kSmemBytes, stream>>>(ta, tw, bias, out, M, N, K, ldo, err);
+  return check_launch("gemm_tn_kernel");
+}
+
+}  // namespace
+
+int device_sm_count(int device) {
+  static int counts[64] = {};
+  if (device < 0 || device >= 64) return 148;
+  if (counts[device] == 0) {
+    int c = 0;
+    if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || c <= 0) c = 148;
+    counts[device] = c;
+  }
+  return counts[device];
+}
+
+gdc_status launch_linear(const __half* a, int64_t lda, const __half* w, const __half* bias, __half* out,
+                         int64_t ldo, int64_t M, int N, int K, int act, cudaStream_t stream, int* err) {
+  if (M <= 0) return GDC_OK;
+  if (N <= 0 || K <= 0 || N % 128 != 0 || K % kBK != 0)
+    return set_error(GDC_ERR_UNSUPPORTED, "linear: N=%d must be a multiple of 128 and K=%d of 64", N, K);
+  if (M > (int64_t(1) << 30)) return set_error(GDC_ERR_UNSUPPORTED, "linear: M too large");
+  if ((lda % 8) || (ldo % 8) || (reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(bias) & 15))
+    return set_error(GDC_ERR_INVALID_INPUT, "linear: pointers must be 16-byte aligned and strides multiples of 8");
+  if (act < 0 || act > 2) return set_error(GDC_ERR_INVALID_INPUT, "linear: unknown activation %d", act);
+  const int bn = (N % 256 == 0) ? 256 : 128;
+  CUtensorMap ta, tw;
+  GDC_TRY(make_tmap(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), kBM));
+  GDC_TRY(make_tmap(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn)));
+  const int m = int(M);
+  if (bn == 256) {
+    if (act == kActGelu) return launch_gemm_variant<256, kActGelu>(ta, tw, bias, out, ldo, m, N, K, stream, err);
+    if (act == kActRelu) return launch_gemm_variant<256, kActRelu>(ta, tw, bias, out, ldo, m, N, K, stream, err);
+    return launch_gemm_variant<256, kActNone>(ta, tw, bias, out, ldo, m, N, K, stream, err);
+  }
+  if (act == kActGelu) return launch_gemm_variant<128, kActGelu>(ta, tw, bias, out, ldo, m, N, K, stream, err);
+  if (act == kActRelu) return launch_gemm_variant<128, kActRelu>(ta, tw, bias, out, ldo, m, N, K, stream, err);
+  return launch_gemm_variant<128, kActNone>(ta, tw, bias, out, ldo, m, N, K, stream, err);
+}
+
+}  // namespace gdc

@@ -1,0 +1,56 @@
+// Host-side launchers for the sm_100a kernels of the forward.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../common.h"
+
+namespace gdc {
+
+// Activation fused into the GEMM epilogue.
+enum Act : int { kActNone = 0, kActGelu = 1, kActRelu = 2 };
+
+// out[M, N] = act(a[M, K] . w[N, K]^T + bias[N]), fp16 in/out, fp32 accumulate, on
+// tcgen05 tensor cores (persistent warp-specialised kernel, TMA-fed).
+// Requirements: N % 128 == 0, K % 64 == 0, lda/ldo multiples of 8 elements,
+// 16-byte aligned pointers. err: device error word (timeouts).
+gdc_status launch_linear(const __half* a, int64_t lda, const __half* w, const __half* bias, __half* out,
+                         int64_t ldo, int64_t M, int N, int K, int act, cudaStream_t stream, int* err);
+
+// out = LN(x + residual) * gamma + beta (rows x cols, fp16; fp32 statistics). The
+// sum x + residual is rounded to fp16 first, as the reference's fp16 add does.
+// residual may be null. cols % 256 == 0, cols <= 4096.
+gdc_status launch_residual_layer_norm(const __half* x, const __half* residual, const __half* gamma,
+                                      const __half* beta, __half* out, int64_t rows, int cols, float eps,
+                                      cudaStream_t stream);
+
+// hidden[t] = LN(E[ids[t]]) * mask[t] for t < rows (DeBERTa.swift:285-292). Ids outside
+// [0, vocab) set kErrBadTokenId and read row 0.
+gdc_status launch_embedding(const int32_t* ids, const __half* mask, const __half* table, int64_t vocab,
+                            const __half* gamma, const __half* beta, __half* out, int64_t rows, int cols,
+                            float eps, cudaStream_t stream, int* err);
+
+// Disentangled attention over the fused QKV projection output (see gdc.h).
+// rel_table: 1023 int32 gather indices (device).
+gdc_status launch_attention(const __half* qkv, const __half* pos_qk, const __half* key_mask,
+                            const int32_t* rel_table, __half* ctx, int batch, int seq_len, int heads,
+                            cudaStream_t stream, int* err);
+
+// rows[r] = hidden[marker[r] + (r / per_batch) * seq_len] (DeBERTa.swift:430-436).
+// Marker indices outside [0, seq_len) set kErrBadMarkerIndex and read row 0 of the batch.
+gdc_status launch_marker_gather(const __half* hidden, const int32_t* markers, __half* rows, int n_rows,
+                                int per_batch, int seq_len, int cols, cudaStream_t stream, int* err);
+
+// logits[r] = where(marker_mask[r] > 0, fp16(h[r] . w2 + b2), -10000) (DeBERTa.swift:437-443).
+gdc_status launch_classifier_out(const __half* h, const __half* w2, const __half* b2, const float* marker_mask,
+                                 float* logits, __half* logits_f16, int n_rows, int dc, cudaStream_t stream);
+
+// Per-task softmax / sigmoid decode in fp32 (RawCLI.swift:182-223).
+gdc_status launch_decode(const float* logits, int batch, int max_heads, int max_options, const int32_t* n_labels,
+                         const uint8_t* multi_label, float* probs, uint8_t* selected, cudaStream_t stream);
+
+int device_sm_count(int device);
+
+}  // namespace gdc

@@ -1,0 +1,167 @@
+// Row LayerNorm kernels: residual-add LayerNorm and the fused embedding stage.
+//
+// residual LN replaces `norm(x + residual)` (DeBERTa.swift:449-464, MLXFast.layerNorm)
+// and FusedKernels.residualLayerNorm (FusedKernels.swift:125-155): one warp per row,
+// 16-byte loads (8 fp16 per lane per chunk), the row held in registers, two-pass
+// mean / biased variance in fp32, rsqrt(var + eps), affine, fp16 store.
+//
+// The embedding kernel replaces DeBERTa.swift:285-292: gather the word-embedding row of
+// each token id, LayerNorm it, multiply by the attention-mask value.
+//
+// Both are HBM-bound: per row they move cols * 2 bytes per input and output once.
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace gdc {
+namespace {
+
+constexpr int kRowsPerBlock = 8;  // 8 warps, one row each
+
+template <int CH>
+__device__ __forceinline__ void ln_row_store(float (&v)[CH * 8], const __half* __restrict__ gamma,
+                                             const __half* __restrict__ beta, __half* __restrict__ dst, int lane,
+                                             float eps, float scale_after) {
+  constexpr int cols = CH * 256;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < CH * 8; ++i) s += v[i];
+  const float mean = ptx::warp_sum(s) * (1.0f / cols);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < CH * 8; ++i) {
+    const float d = v[i] - mean;
+    q += d * d;
+  }
+  const float var = ptx::warp_sum(q) * (1.0f / cols);
+  const float inv = rsqrtf(var + eps);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gamma + col));
+    const uint4 bv = __ldg(reinterpret_cast<const uint4*>(beta + col));
+    const __half2* gh = reinterpret_cast<const __half2*>(&gv);
+    const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 g = __half22float2(gh[j]);
+      const float2 b = __half22float2(bh[j]);
+      float y0 = (v[c * 8 + 2 * j] - mean) * inv * g.x + b.x;
+      float y1 = (v[c * 8 + 2 * j + 1] - mean) * inv * g.y + b.y;
+      if (scale_after != 1.0f) {
+        // LN output is rounded to fp16 before the mask multiply (two fp16 ops).
+        y0 = __half2float(__float2half_rn(y0)) * scale_after;
+        y1 = __half2float(__float2half_rn(y1)) * scale_after;
+      }
+      o[j] = ptx::pack_half2(y0, y1);
+    }
+    *reinterpret_cast<uint4*>(dst + col) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int CH>
+__global__ void __launch_bounds__(kRowsPerBlock * 32)
+    residual_ln_kernel(const __half* __restrict__ x, const __half* __restrict__ res, const __half* __restrict__ gamma,
+                       const __half* __restrict__ beta, __half* __restrict__ out, long long rows, float eps) {
+  constexpr int cols = CH * 256;
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const __half* xr = x + row * cols;
+  float v[CH * 8];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + col);
+    const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+    if (res != nullptr) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(res + row * cols + col);
+      const __half2* rh = reinterpret_cast<const __half2*>(&rv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 s = __half22float2(__hadd2(xh[j], rh[j]));  // fp16 add, as the reference
+        v[c * 8 + 2 * j] = s.x;
+        v[c * 8 + 2 * j + 1] = s.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 s = __half22float2(xh[j]);
+        v[c * 8 + 2 * j] = s.x;
+        v[c * 8 + 2 * j + 1] = s.y;
+      }
+    }
+  }
+  ln_row_store<CH>(v, gamma, beta, out + row * cols, lane, eps, 1.0f);
+}
+
+template <int CH>
+__global__ void __launch_bounds__(kRowsPerBlock * 32)
+    embedding_kernel(const int32_t* __restrict__ ids, const __half* __restrict__ mask, const __half* __restrict__ table,
+                     long long vocab, const __half* __restrict__ gamma, const __half* __restrict__ beta,
+                     __half* __restrict__ out, long long rows, float eps, int* err) {
+  constexpr int cols = CH * 256;
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  long long id = ids[row];
+  if (id < 0 || id >= vocab) {
+    if (lane == 0) atomicOr(err, kErrBadTokenId);
+    id = 0;
+  }
+  const __half* er = table + id * cols;
+  float v[CH * 8];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    const uint4 ev = __ldg(reinterpret_cast<const uint4*>(er + col));
+    const __half2* eh = reinterpret_cast<const __half2*>(&ev);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 s = __half22float2(eh[j]);
+      v[c * 8 + 2 * j] = s.x;
+      v[c * 8 + 2 * j + 1] = s.y;
+    }
+  }
+  const float m = __half2float(mask[row]);
+  // scale_after == 1 would skip the rounding; a mask of exactly 1 changes nothing anyway.
+  ln_row_store<CH>(v, gamma, beta, out + row * cols, lane, eps, m);
+}
+
+}  // namespace
+
+#define GDC_LN_DISPATCH(CH_EXPR, KERNEL, ...)                                                 \
+  switch (CH_EXPR) {                                                                          \
+    case 1: KERNEL<1><<<grid, kRowsPerBlock * 32, 0, stream>>>(__VA_ARGS__); break;          \
+    case 2: KERNEL<2><<<grid, kRowsPerBlock * 32, 0, stream>>>(__VA_ARGS__); break;          \
+    case 3: KERNEL<3><<<grid, kRowsPerBlock * 32, 0, stream>>>(__VA_ARGS__); break;          \
+    case 4: KERNEL<4><<<grid, kRowsPerBlock * 32, 0, stream>>>(__VA_ARGS__); break;          \
+    case 8: KERNEL<8><<<grid, kRowsPerBlock * 32, 0, stream>>>(__VA_ARGS__); break;          \
+    case 16: KERNEL<16><<<grid, kRowsPerBlock * 32, 0, stream>>>(__VA_ARGS__); break;        \
+    default: return set_error(GDC_ERR_UNSUPPORTED, "layer norm: cols=%d unsupported", cols); \
+  }
+
+gdc_status launch_residual_layer_norm(const __half* x, const __half* residual, const __half* gamma,
+                                      const __half* beta, __half* out, int64_t rows, int cols, float eps,
+                                      cudaStream_t stream) {
+  if (rows <= 0) return GDC_OK;
+  if (cols <= 0 || cols % 256 != 0 || cols > 4096)
+    return set_error(GDC_ERR_UNSUPPORTED, "layer norm: cols=%d must be a multiple of 256 and <= 4096", cols);
+  const unsigned grid = unsigned((rows + kRowsPerBlock - 1) / kRowsPerBlock);
+  GDC_LN_DISPATCH(cols / 256, residual_ln_kernel, x, residual, gamma, beta, out, (long long)rows, eps);
+  return check_launch("residual_ln_kernel");
+}
+
+gdc_status launch_embedding(const int32_t* ids, const __half* mask, const __half* table, int64_t vocab,
+                            const __half* gamma, const __half* beta, __half* out, int64_t rows, int cols,
+                            float eps, cudaStream_t stream, int* err) {
+  if (rows <= 0) return GDC_OK;
+  if (cols <= 0 || cols % 256 != 0 || cols > 4096)
+    return set_error(GDC_ERR_UNSUPPORTED, "embedding: cols=%d unsupported", cols);
+  const unsigned grid = unsigned((rows + kRowsPerBlock - 1) / kRowsPerBlock);
+  GDC_LN_DISPATCH(cols / 256, embedding_kernel, ids, mask, table, (long long)vocab, gamma, beta, out,
+                  (long long)rows, eps, err);
+  return check_launch("embedding_kernel");
+}
+
+}  // namespace gdc

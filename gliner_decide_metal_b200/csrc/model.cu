@@ -1,0 +1,415 @@
+// Model load and forward orchestration.
+//
+// Load follows GLiNERDecideClassifier.init (DeBERTa.swift:188-242): every tensor is read
+// from one safetensors file with the reference's key names, the QKV weights are
+// concatenated q | k | v (DeBERTa.swift:129-136), LN(rel_embeddings) and the per-layer
+// relative projections [PQ | PK] = LN(rel) [Wq; Wk]^T + [bq; bk] are computed once on the
+// device with the same GEMM kernel the forward uses (DeBERTa.swift:204-227).
+//
+// The forward (DeBERTa.swift:274-447) runs on one CUDA stream with no host
+// synchronisation: embedding -> 24 x (QKV GEMM, attention, out-proj GEMM, residual LN,
+// FFN-up GEMM + GELU, FFN-down GEMM, residual LN) -> marker gather -> classifier GEMM +
+// ReLU -> classifier dot + mask.
+#include "model.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "kernels/kernels.h"
+#include "safetensors.h"
+
+namespace gdc {
+
+gdc_status launch_attention_simt(const __half* qkv, const __half* pos_qk, const __half* key_mask,
+                                 const int32_t* rel_table, __half* ctx, int batch, int seq_len, int heads,
+                                 cudaStream_t stream);
+
+const char* profile_class_name(int c) {
+  static const char* names[kProfCount] = {"embedding",  "qkv_gemm",      "attention",       "out_gemm",
+                                          "layer_norm", "ffn_up_gemm",   "ffn_down_gemm",   "classifier"};
+  return (c >= 0 && c < kProfCount) ? names[c] : "?";
+}
+
+void build_relative_table(int position_buckets, int max_relative_positions, int32_t* table) {
+  // DeBERTa.swift:526-547 in double precision, then clip(bucket + 256, 0, 511)
+  // (DeBERTa.swift:507-515). Index r + 511 for r = q - k in [-511, 511].
+  const int mid = position_buckets / 2;
+  const int span = position_buckets;
+  for (int r = -511; r <= 511; ++r) {
+    int abs_pos = (r > -mid && r < mid) ? mid - 1 : (r < 0 ? -r : r);
+    const double lp = std::ceil(std::log(double(abs_pos) / double(mid)) /
+                                std::log(double(max_relative_positions - 1) / double(mid)) * double(mid - 1));
+    const int log_pos = int(lp) + mid;
+    const int bucket = abs_pos <= mid ? r : log_pos * (r < 0 ? -1 : 1);
+    int idx = bucket + span;
+    if (idx < 0) idx = 0;
+    if (idx > 2 * span - 1) idx = 2 * span - 1;
+    table[r + 511] = idx;
+  }
+}
+
+namespace {
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct PendingUpload {
+  __half** dst;
+  std::vector<uint16_t> host;
+};
+
+}  // namespace
+
+gdc_status model_load(const char* path, const gdc_config* cfg_in, int device, gdc_model** out) {
+  if (!path || !out) return set_error(GDC_ERR_NULL_POINTER, "gdc_model_load: null argument");
+  *out = nullptr;
+  gdc_config cfg;
+  gdc_config_default(&cfg);
+  if (cfg_in) cfg = *cfg_in;
+  if (cfg.num_attention_heads <= 0 || cfg.hidden_size != cfg.num_attention_heads * 64)
+    return set_error(GDC_ERR_UNSUPPORTED, "hidden_size must equal 64 * num_attention_heads (got %d, %d)",
+                     cfg.hidden_size, cfg.num_attention_heads);
+  if (cfg.hidden_size % 256 != 0 || cfg.hidden_size > 4096 || cfg.intermediate_size % 256 != 0 ||
+      cfg.intermediate_size <= 0)
+    return set_error(GDC_ERR_UNSUPPORTED, "hidden/intermediate sizes must be multiples of 256 (hidden <= 4096)");
+  if (cfg.num_hidden_layers <= 0) return set_error(GDC_ERR_UNSUPPORTED, "num_hidden_layers must be positive");
+  if (cfg.position_buckets != 256)
+    return set_error(GDC_ERR_UNSUPPORTED, "position_buckets must be 256 (512-row relative table)");
+  if (cfg.vocab_size <= 0) return set_error(GDC_ERR_UNSUPPORTED, "vocab_size must be positive");
+
+  // Parse and validate the whole file on the host first: key / shape / dtype errors are
+  // reported without touching the device.
+  SafetensorsFile file;
+  GDC_TRY(file.open(path));
+
+  const int64_t E = cfg.hidden_size, F = cfg.intermediate_size;
+  auto m = new gdc_model();
+  m->device = device;
+  m->cfg = cfg;
+  m->hidden = int(E);
+  m->heads = cfg.num_attention_heads;
+  m->inter = int(F);
+  m->layers_n = cfg.num_hidden_layers;
+  m->vocab = cfg.vocab_size;
+  m->eps = cfg.layer_norm_eps;
+  m->layers.resize(size_t(cfg.num_hidden_layers));
+
+  std::vector<PendingUpload> ups;
+  gdc_status st = GDC_OK;
+  auto get = [&](const std::string& key, std::vector<int64_t> shape, __half** dst) -> gdc_status {
+    PendingUpload u;
+    u.dst = dst;
+    gdc_status s = file.get_f16(key, &shape, &u.host);
+    if (s != GDC_OK) return s;
+    ups.push_back(std::move(u));
+    return GDC_OK;
+  };
+
+  // classifier width from the file (DeBERTa.swift:228-229 does not constrain it)
+  const TensorInfo* c0 = file.info("classifier.0.weight");
+  if (!c0) {
+    delete m;
+    return set_error(GDC_ERR_MISSING_WEIGHT, "Missing model weight: classifier.0.weight");
+  }
+  if (c0->shape.size() != 2 || c0->shape[1] != E || c0->shape[0] <= 0 || c0->shape[0] % 256 != 0) {
+    delete m;
+    return set_error(GDC_ERR_INVALID_SHAPE, "Weight classifier.0.weight must be [d_c, %lld] with d_c %% 256 == 0",
+                     (long long)E);
+  }
+  const int64_t DC = c0->shape[0];
+  m->classifier_hidden = int(DC);
+
+  do {
+    if ((st = get("encoder.embeddings.word_embeddings.weight", {cfg.vocab_size, E}, &m->word_emb))) break;
+    if ((st = get("encoder.embeddings.LayerNorm.weight", {E}, &m->emb_ln_g))) break;
+    if ((st = get("encoder.embeddings.LayerNorm.bias", {E}, &m->emb_ln_b))) break;
+    if ((st = get("encoder.encoder.rel_embeddings.weight", {512, E}, &m->rel_ln))) break;
+    for (int i = 0; i < cfg.num_hidden_layers && st == GDC_OK; ++i) {
+      const std::string p = "encoder.encoder.layer." + std::to_string(i);
+      LayerWeights& L = m->layers[size_t(i)];
+      // q, k, v are concatenated into one [3E, E] matrix below.
+      std::vector<uint16_t> wq, wk, wv, bq, bk, bv;
+      std::vector<int64_t> sw = {E, E}, sb = {E};
+      if ((st = file.get_f16(p + ".attention.self.query_proj.weight", &sw, &wq))) break;
+      if ((st = file.get_f16(p + ".attention.self.key_proj.weight", &sw, &wk))) break;
+      if ((st = file.get_f16(p + ".attention.self.value_proj.weight", &sw, &wv))) break;
+      if ((st = file.get_f16(p + ".attention.self.query_proj.bias", &sb, &bq))) break;
+      if ((st = file.get_f16(p + ".attention.self.key_proj.bias", &sb, &bk))) break;
+      if ((st = file.get_f16(p + ".attention.self.value_proj.bias", &sb, &bv))) break;
+      PendingUpload uw, ub;
+      uw.dst = &L.wqkv;
+      uw.host.reserve(wq.size() * 3);
+      uw.host.insert(uw.host.end(), wq.begin(), wq.end());
+      uw.host.insert(uw.host.end(), wk.begin(), wk.end());
+      uw.host.insert(uw.host.end(), wv.begin(), wv.end());
+      ub.dst = &L.bqkv;
+      ub.host.insert(ub.host.end(), bq.begin(), bq.end());
+      ub.host.insert(ub.host.end(), bk.begin(), bk.end());
+      ub.host.insert(ub.host.end(), bv.begin(), bv.end());
+      ups.push_back(std::move(uw));
+      ups.push_back(std::move(ub));
+      if ((st = get(p + ".attention.output.dense.weight", {E, E}, &L.wo))) break;
+      if ((st = get(p + ".attention.output.dense.bias", {E}, &L.bo))) break;
+      if ((st = get(p + ".attention.output.LayerNorm.weight", {E}, &L.ln1_g))) break;
+      if ((st = get(p + ".attention.output.LayerNorm.bias", {E}, &L.ln1_b))) break;
+      if ((st = get(p + ".intermediate.dense.weight", {F, E}, &L.w1))) break;
+      if ((st = get(p + ".intermediate.dense.bias", {F}, &L.b1))) break;
+      if ((st = get(p + ".output.dense.weight", {E, F}, &L.w2))) break;
+      if ((st = get(p + ".output.dense.bias", {E}, &L.b2))) break;
+      if ((st = get(p + ".output.LayerNorm.weight", {E}, &L.ln2_g))) break;
+      if ((st = get(p + ".output.LayerNorm.bias", {E}, &L.ln2_b))) break;
+    }
+    if (st) break;
+    if ((st = get("classifier.0.weight", {DC, E}, &m->cls_w0))) break;
+    if ((st = get("classifier.0.bias", {DC}, &m->cls_b0))) break;
+    if ((st = get("classifier.2.weight", {1, DC}, &m->cls_w2))) break;
+    if ((st = get("classifier.2.bias", {1}, &m->cls_b2))) break;
+  } while (false);
+  // LN(rel) scratch: the encoder LN params are needed only at load.
+  std::vector<uint16_t> rel_g, rel_b;
+  if (st == GDC_OK) {
+    std::vector<int64_t> sb = {E};
+    st = file.get_f16("encoder.encoder.LayerNorm.weight", &sb, &rel_g);
+    if (st == GDC_OK) st = file.get_f16("encoder.encoder.LayerNorm.bias", &sb, &rel_b);
+  }
+  if (st != GDC_OK) {
+    delete m;
+    return st;
+  }
+
+  int ndev = 0;
+  cudaError_t dc = cudaGetDeviceCount(&ndev);
+  if (dc != cudaSuccess || device < 0 || device >= ndev) {
+    delete m;
+    return set_error(GDC_ERR_CUDA, "CUDA device %d not available (%s, %d devices)", device,
+                     dc == cudaSuccess ? "ok" : cudaGetErrorString(dc), ndev);
+  }
+
+  // One pool: uploaded tensors, per-layer [512, 2E] relative projections, LN(rel) params,
+  // relative table and the error word.
+  size_t total = 0;
+  for (auto& u : ups) total += align256(u.host.size() * 2);
+  const size_t pos_bytes = align256(size_t(512) * 2 * E * 2);
+  total += pos_bytes * size_t(cfg.num_hidden_layers);
+  total += align256(E * 2) * 2 + align256(size_t(512) * E * 2) + align256(1023 * 4) + 256;
+
+  auto fail = [&](gdc_status s) {
+    model_free(m);
+    return s;
+  };
+  cudaError_t ce = cudaSetDevice(device);
+  if (ce != cudaSuccess) {
+    delete m;
+    return set_error(GDC_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(ce));
+  }
+  ce = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+  if (ce != cudaSuccess) {
+    delete m;
+    return set_error(GDC_ERR_CUDA, "cudaStreamCreate: %s", cudaGetErrorString(ce));
+  }
+  ce = cudaMalloc(&m->weight_pool, total);
+  if (ce != cudaSuccess) {
+    m->weight_pool = nullptr;
+    return fail(set_error(GDC_ERR_OUT_OF_MEMORY, "cudaMalloc(%zu) for weights: %s", total, cudaGetErrorString(ce)));
+  }
+  uint8_t* cur = static_cast<uint8_t*>(m->weight_pool);
+  for (auto& u : ups) {
+    *u.dst = reinterpret_cast<__half*>(cur);
+    ce = cudaMemcpy(cur, u.host.data(), u.host.size() * 2, cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) return fail(set_error(GDC_ERR_CUDA, "weight upload: %s", cudaGetErrorString(ce)));
+    cur += align256(u.host.size() * 2);
+  }
+  for (auto& L : m->layers) {
+    L.pos_qk = reinterpret_cast<__half*>(cur);
+    cur += pos_bytes;
+  }
+  __half* rel_g_d = reinterpret_cast<__half*>(cur);
+  cur += align256(E * 2);
+  __half* rel_b_d = reinterpret_cast<__half*>(cur);
+  cur += align256(E * 2);
+  __half* rel_norm = reinterpret_cast<__half*>(cur);
+  cur += align256(size_t(512) * E * 2);
+  m->rel_table = reinterpret_cast<int32_t*>(cur);
+  cur += align256(1023 * 4);
+  m->err = reinterpret_cast<int*>(cur);
+
+  int32_t table[1023];
+  build_relative_table(cfg.position_buckets, 512, table);
+  if ((ce = cudaMemcpy(m->rel_table, table, sizeof(table), cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (ce = cudaMemcpy(rel_g_d, rel_g.data(), E * 2, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (ce = cudaMemcpy(rel_b_d, rel_b.data(), E * 2, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (ce = cudaMemset(m->err, 0, 256)) != cudaSuccess)
+    return fail(set_error(GDC_ERR_CUDA, "model upload: %s", cudaGetErrorString(ce)));
+
+  // LN(rel_embeddings) (DeBERTa.swift:209-213) -> rel_norm; then per layer
+  // [PQ | PK] = rel_norm . Wqkv[0:2E]^T + bqkv[0:2E] (DeBERTa.swift:218-227).
+  st = launch_residual_layer_norm(m->rel_ln, nullptr, rel_g_d, rel_b_d, rel_norm, 512, int(E), m->eps, m->stream);
+  if (st != GDC_OK) return fail(st);
+  for (auto& L : m->layers) {
+    st = launch_linear(rel_norm, E, L.wqkv, L.bqkv, L.pos_qk, 2 * E, 512, int(2 * E), int(E), kActNone, m->stream,
+                       m->err);
+    if (st != GDC_OK) return fail(st);
+  }
+  // keep LN(rel) as the model's relative table copy (rel_ln aliases the raw upload slot)
+  ce = cudaMemcpyAsync(m->rel_ln, rel_norm, size_t(512) * E * 2, cudaMemcpyDeviceToDevice, m->stream);
+  if (ce != cudaSuccess) return fail(set_error(GDC_ERR_CUDA, "copy: %s", cudaGetErrorString(ce)));
+  st = read_device_errors(m, m->stream);
+  if (st != GDC_OK) return fail(st);
+  *out = m;
+  return GDC_OK;
+}
+
+void model_free(gdc_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  Workspace& w = m->ws;
+  for (void* p : {(void*)w.x, (void*)w.x1, (void*)w.big, (void*)w.ctx, (void*)w.tmp, (void*)w.mrows,
+                  (void*)w.mhid, (void*)w.ids, (void*)w.mask, (void*)w.marker_idx, (void*)w.marker_mask,
+                  (void*)w.logits, (void*)w.logits16})
+    if (p) cudaFree(p);
+  if (w.h_in) cudaFreeHost(w.h_in);
+  if (w.h_out) cudaFreeHost(w.h_out);
+  for (auto e : m->events) cudaEventDestroy(e);
+  if (m->weight_pool) cudaFree(m->weight_pool);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+gdc_status ensure_workspace(gdc_model* m, int64_t tokens, int64_t markers) {
+  Workspace& w = m->ws;
+  const int64_t E = m->hidden;
+  const int64_t big_cols = std::max<int64_t>(3 * E, m->inter);
+  auto grow = [](void** p, size_t bytes) -> gdc_status {
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) {
+      *p = nullptr;
+      return set_error(GDC_ERR_OUT_OF_MEMORY, "workspace cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    }
+    return GDC_OK;
+  };
+  if (tokens > w.tokens) {
+    // grow geometrically to avoid reallocation churn across buckets
+    int64_t cap = std::max<int64_t>(tokens, w.tokens * 2);
+    cudaStreamSynchronize(m->stream);
+    GDC_TRY(grow((void**)&w.x, size_t(cap) * E * 2));
+    GDC_TRY(grow((void**)&w.x1, size_t(cap) * E * 2));
+    GDC_TRY(grow((void**)&w.big, size_t(cap) * big_cols * 2));
+    GDC_TRY(grow((void**)&w.ctx, size_t(cap) * E * 2));
+    GDC_TRY(grow((void**)&w.tmp, size_t(cap) * E * 2));
+    GDC_TRY(grow((void**)&w.ids, size_t(cap) * 4));
+    GDC_TRY(grow((void**)&w.mask, size_t(cap) * 2));
+    w.tokens = cap;
+  }
+  if (markers > w.markers) {
+    int64_t cap = std::max<int64_t>(markers, w.markers * 2);
+    cudaStreamSynchronize(m->stream);
+    GDC_TRY(grow((void**)&w.mrows, size_t(cap) * E * 2));
+    GDC_TRY(grow((void**)&w.mhid, size_t(cap) * m->classifier_hidden * 2));
+    GDC_TRY(grow((void**)&w.marker_idx, size_t(cap) * 4));
+    GDC_TRY(grow((void**)&w.marker_mask, size_t(cap) * 4));
+    GDC_TRY(grow((void**)&w.logits, size_t(cap) * 4));
+    GDC_TRY(grow((void**)&w.logits16, size_t(cap) * 2));
+    w.markers = cap;
+  }
+  return GDC_OK;
+}
+
+namespace {
+
+// Records an event after the kernels of `cls` when profiling.
+struct StageRecorder {
+  gdc_model* m;
+  cudaStream_t s;
+  bool on;
+  bool named;
+  void begin() {
+    if (!on) return;
+    if (m->events_used < m->events.size()) {
+      cudaEventRecord(m->events[m->events_used], s);
+      m->event_class[m->events_used] = -1;
+      ++m->events_used;
+    }
+  }
+  void end(int cls, const std::string& name) {
+    if (!on) return;
+    if (m->events_used < m->events.size()) {
+      cudaEventRecord(m->events[m->events_used], s);
+      m->event_class[m->events_used] = cls;
+      ++m->events_used;
+      if (named) m->stage_names.push_back(name);
+    }
+  }
+};
+
+}  // namespace
+
+gdc_status forward(gdc_model* m, int B, int L, int Hm, int O, const int32_t* ids, const __half* mask,
+                   const int32_t* markers, const float* marker_mask, float* logits, __half* logits16,
+                   cudaStream_t s, bool named_stages) {
+  const int64_t T = int64_t(B) * L;
+  const int64_t R = int64_t(B) * Hm * O;
+  const int E = m->hidden, F = m->inter;
+  GDC_TRY(ensure_workspace(m, T, R));
+  Workspace& w = m->ws;
+  StageRecorder rec{m, s, m->profiling || named_stages, named_stages};
+  if (rec.on) {
+    // one event after every kernel group; make sure the pool is large enough
+    const size_t need = m->events_used + size_t(7 * m->layers_n + 4);
+    while (m->events.size() < need) {
+      cudaEvent_t e;
+      GDC_CUDA_TRY(cudaEventCreate(&e));
+      m->events.push_back(e);
+      m->event_class.push_back(-1);
+    }
+  }
+  rec.begin();
+  GDC_TRY(launch_embedding(ids, mask, m->word_emb, m->vocab, m->emb_ln_g, m->emb_ln_b, w.x, T, E, m->eps, s, m->err));
+  rec.end(kProfEmbedding, "embedding");
+  for (int i = 0; i < m->layers_n; ++i) {
+    const LayerWeights& Lw = m->layers[size_t(i)];
+    const std::string p = "layer_" + std::to_string(i) + "_";
+    GDC_TRY(launch_linear(w.x, E, Lw.wqkv, Lw.bqkv, w.big, 3 * E, T, 3 * E, E, kActNone, s, m->err));
+    rec.end(kProfQkvGemm, p + "attention_projection");
+    GDC_TRY(launch_attention(w.big, Lw.pos_qk, mask, m->rel_table, w.ctx, B, L, m->heads, s, m->err));
+    rec.end(kProfAttention, p + "attention");
+    GDC_TRY(launch_linear(w.ctx, E, Lw.wo, Lw.bo, w.tmp, E, T, E, E, kActNone, s, m->err));
+    rec.end(kProfOutGemm, "");
+    GDC_TRY(launch_residual_layer_norm(w.tmp, w.x, Lw.ln1_g, Lw.ln1_b, w.x1, T, E, m->eps, s));
+    rec.end(kProfLayerNorm, p + "attention_output");
+    GDC_TRY(launch_linear(w.x1, E, Lw.w1, Lw.b1, w.big, F, T, F, E, kActGelu, s, m->err));
+    rec.end(kProfFfnUpGemm, "");
+    GDC_TRY(launch_linear(w.big, F, Lw.w2, Lw.b2, w.tmp, E, T, E, F, kActNone, s, m->err));
+    rec.end(kProfFfnDownGemm, "");
+    GDC_TRY(launch_residual_layer_norm(w.tmp, w.x1, Lw.ln2_g, Lw.ln2_b, w.x, T, E, m->eps, s));
+    rec.end(kProfLayerNorm, p + "feed_forward");
+  }
+  GDC_TRY(launch_marker_gather(w.x, markers, w.mrows, int(R), Hm * O, L, E, s, m->err));
+  GDC_TRY(launch_linear(w.mrows, E, m->cls_w0, m->cls_b0, w.mhid, m->classifier_hidden, R, m->classifier_hidden, E,
+                        kActRelu, s, m->err));
+  GDC_TRY(launch_classifier_out(w.mhid, m->cls_w2, m->cls_b2, marker_mask, logits, logits16, int(R),
+                                m->classifier_hidden, s));
+  rec.end(kProfClassifier, "classifier");
+  return GDC_OK;
+}
+
+gdc_status read_device_errors(gdc_model* m, cudaStream_t s) {
+  int h = 0;
+  GDC_CUDA_TRY(cudaMemcpyAsync(&h, m->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  GDC_CUDA_TRY(cudaStreamSynchronize(s));
+  if (h != 0) {
+    GDC_CUDA_TRY(cudaMemsetAsync(m->err, 0, sizeof(int), s));
+    GDC_CUDA_TRY(cudaStreamSynchronize(s));
+    if (h & kErrTimeout)
+      return set_error(GDC_ERR_TIMEOUT, "a device-side wait exceeded its time limit (error word 0x%x)", h);
+    if (h & kErrBadTokenId) return set_error(GDC_ERR_INVALID_INPUT, "input id outside [0, vocab) (device check)");
+    if (h & kErrBadMarkerIndex)
+      return set_error(GDC_ERR_INVALID_INPUT, "marker index outside [0, seq_len) (device check)");
+    return set_error(GDC_ERR_CUDA, "device error word 0x%x", h);
+  }
+  return GDC_OK;
+}
+
+}  // namespace gdc

@@ -1,0 +1,134 @@
+// Device-resident model: weights, per-layer relative projections, workspace and the
+// forward pass of GLiNERDecideClassifier (DeBERTa.swift:156-447).
+#pragma once
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "common.h"
+
+namespace gdc {
+
+struct LayerWeights {
+  __half* wqkv = nullptr;  // [3E, E] rows q | k | v (DeBERTa.swift:129-136)
+  __half* bqkv = nullptr;  // [3E]
+  __half* wo = nullptr;    // [E, E]
+  __half* bo = nullptr;
+  __half* ln1_g = nullptr;
+  __half* ln1_b = nullptr;
+  __half* w1 = nullptr;    // [F, E]
+  __half* b1 = nullptr;
+  __half* w2 = nullptr;    // [E, F]
+  __half* b2 = nullptr;
+  __half* ln2_g = nullptr;
+  __half* ln2_b = nullptr;
+  __half* pos_qk = nullptr;  // [512, 2E]: PQ | PK (DeBERTa.swift:218-227)
+};
+
+// Kernel groups recorded by the stage profiler.
+enum ProfileClass : int {
+  kProfEmbedding = 0,
+  kProfQkvGemm,
+  kProfAttention,
+  kProfOutGemm,
+  kProfLayerNorm,
+  kProfFfnUpGemm,
+  kProfFfnDownGemm,
+  kProfClassifier,
+  kProfCount
+};
+
+const char* profile_class_name(int c);
+
+struct Workspace {
+  int64_t tokens = 0;   // capacity in B*L rows
+  int64_t markers = 0;  // capacity in B*Hm*O rows
+  __half* x = nullptr;      // [T, E] hidden
+  __half* x1 = nullptr;     // [T, E] hidden after the attention block
+  __half* big = nullptr;    // [T, max(3E, F)] QKV projection, later FFN intermediate
+  __half* ctx = nullptr;    // [T, E]
+  __half* tmp = nullptr;    // [T, E] projection outputs before residual LN
+  __half* mrows = nullptr;  // [R, E] gathered marker rows
+  __half* mhid = nullptr;   // [R, dc] classifier hidden
+  // input / output staging (device)
+  int32_t* ids = nullptr;
+  __half* mask = nullptr;
+  int32_t* marker_idx = nullptr;
+  float* marker_mask = nullptr;
+  float* logits = nullptr;
+  __half* logits16 = nullptr;
+  // pinned host staging
+  uint8_t* h_in = nullptr;
+  size_t h_in_bytes = 0;
+  uint8_t* h_out = nullptr;
+  size_t h_out_bytes = 0;
+};
+
+}  // namespace gdc
+
+struct gdc_model {
+  int device = 0;
+  gdc_config cfg{};
+  int hidden = 1024;
+  int heads = 16;
+  int inter = 4096;
+  int layers_n = 24;
+  int64_t vocab = 128011;
+  int classifier_hidden = 2048;
+  float eps = 1e-7f;
+
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+
+  void* weight_pool = nullptr;
+  __half* word_emb = nullptr;
+  __half* emb_ln_g = nullptr;
+  __half* emb_ln_b = nullptr;
+  __half* rel_ln = nullptr;  // LN(rel_embeddings) [512, E]
+  __half* cls_w0 = nullptr;
+  __half* cls_b0 = nullptr;
+  __half* cls_w2 = nullptr;
+  __half* cls_b2 = nullptr;
+  std::vector<gdc::LayerWeights> layers;
+  int32_t* rel_table = nullptr;  // [1023]
+  int* err = nullptr;            // device error word
+
+  gdc::Workspace ws;
+
+  // stage profiler (events bracket kernel groups)
+  bool profiling = false;
+  std::vector<cudaEvent_t> events;
+  std::vector<int> event_class;  // class of the interval ending at events[i]
+  size_t events_used = 0;
+  double prof_ns[gdc::kProfCount] = {};
+  int64_t prof_launches[gdc::kProfCount] = {};
+  // named stage events for gdc_classify(collect_profile) (reference stage names)
+  std::vector<std::string> stage_names;
+};
+
+namespace gdc {
+
+gdc_status model_load(const char* path, const gdc_config* cfg, int device, gdc_model** out);
+void model_free(gdc_model* m);
+
+// Ensures workspace for `tokens` rows and `markers` marker rows.
+gdc_status ensure_workspace(gdc_model* m, int64_t tokens, int64_t markers);
+
+// Runs the forward on device-resident inputs (ws or caller buffers) on `stream`.
+// named_stages: record the reference's stage events into m->stage_names / events.
+gdc_status forward(gdc_model* m, int batch, int seq_len, int max_heads, int max_options, const int32_t* ids,
+                   const __half* mask, const int32_t* markers, const float* marker_mask, float* logits,
+                   __half* logits16, cudaStream_t stream, bool named_stages);
+
+// Reads and clears the device error word (synchronises `stream`).
+gdc_status read_device_errors(gdc_model* m, cudaStream_t stream);
+
+// Host-side relative index table (DeBERTa.swift:521-551), 1023 entries.
+void build_relative_table(int position_buckets, int max_relative_positions, int32_t* table);
+
+}  // namespace gdc
