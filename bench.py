@@ -1,0 +1,377 @@
+#!/usr/bin/env python3
+"""Throughput benchmark of the B200 GLiNER2.5-Decide classification forward.
+
+Workload: DeBERTa-v3-large (24 layers) + GLiNER classification MLP,
+batch 32, L=256 bucket, fp16 random-init weights (seed 0), synthetic rows with text
+lengths U[40, 230] and 1 single-label task x 5 labels. A step is one forward pass over
+one such batch. With ``--gpus N`` (launched one process per GPU by torchrun) every rank
+runs its own batches (weak scaling: rows are independent, no collective on the data
+path); timing is device-side (CUDA events on the model's stream), max over ranks.
+
+Printed JSON line (rank 0):
+  value     sequences/s over all ranks, inputs resident in HBM (gdc_classify_device)
+  e2e       the same metric through gdc_classify with host buffers (H2D of the step's
+            inputs and D2H of its logits inside the timed region)
+  roofline  the dominant kernel (the tcgen05 projection GEMM): algorithmic FLOPs / its
+            CUDA-event-measured time inside the timed region, against the measured bf16
+            peak in MEASURED_PEAKS.json
+  cpu_baseline  the CPU restatement of the reference forward (oracle/, numpy fp32 BLAS,
+            all host threads) on a bounded sample of the same workload (rank 0, N=1)
+
+``--impl reference`` times that CPU restatement alone (the reference itself is Swift/MLX
+for Apple silicon and cannot run here) and prints its line with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "sequences/sec, DeBERTa-v3-large b32 L256 fp16, 1/2/4/8 B200; % roofline"
+UNIT = "sequences/sec"
+BATCH, SEQ = 32, 256
+LAYERS = 24
+HIDDEN, INTER = 1024, 4096
+N_RESIDENT_BATCHES = 8
+# Algorithmic FLOPs of the four encoder projections per token (QKV 3072, out 1024,
+# FFN up 4096, FFN down 4096 outputs; K = 1024 / 1024 / 1024 / 4096), 24 layers.
+GEMM_FLOPS_PER_TOKEN = 2 * (3 * HIDDEN * HIDDEN + HIDDEN * HIDDEN + 2 * HIDDEN * INTER) * LAYERS
+ATTN_FLOPS_PER_SEQ = LAYERS * 16 * 4 * 2 * SEQ * SEQ * 64  # QK, c2p, p2c, PV as gathered dots
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
+    ap.add_argument("--weights", type=str, default=None, help="reuse an existing weights file")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d["bf16_tflops_sustained"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def weights_path(rank, world, dist, explicit):
+    if explicit:
+        return Path(explicit)
+    path = Path(tempfile.gettempdir()) / "gdc_bench_weights_seed0_l24.safetensors"
+    if rank == 0 and not path.exists():
+        from gliner_decide_metal_b200 import synthetic
+        tmp = path.with_suffix(".tmp")
+        synthetic.write_weights(tmp, seed=0, num_layers=LAYERS)
+        os.replace(tmp, path)
+    if world > 1:
+        dist.barrier()
+    return path
+
+
+# ----------------------------------------------------------------------------- CPU arm
+
+def cpu_reference_sample(budget_s: float, min_rows: int = 1, max_rows: int = BATCH, seed: int = 3):
+    """Time the oracle's fp32 forward on rows of the benchmark batch, one row per call,
+    until `budget_s` is used. Returns (seq_per_s, rows, seconds, threads)."""
+    from oracle import reference_forward as rf
+    from gliner_decide_metal_b200 import synthetic
+    try:
+        from threadpoolctl import threadpool_limits
+        limiter = threadpool_limits(limits=cpu_threads())
+    except Exception:
+        limiter = None
+    w = synthetic.make_weights(seed=0, num_layers=LAYERS)
+    W = rf.OracleWeights(w, rf.OracleConfig())
+    proj = rf.relative_projections(W, fp16_rounding=False)
+    batch = synthetic.config2(seed=seed)
+    # warm-up one row (BLAS thread pool start-up)
+    rf.forward(W, batch.input_ids[:1], batch.attention_mask[:1], batch.marker_indices[:1], batch.marker_mask[:1],
+               fp16_rounding=False, projections=proj)
+    rows = 0
+    t0 = time.perf_counter()
+    while rows < max_rows and (rows < min_rows or time.perf_counter() - t0 < budget_s):
+        i = rows % BATCH
+        rf.forward(W, batch.input_ids[i:i + 1], batch.attention_mask[i:i + 1], batch.marker_indices[i:i + 1],
+                   batch.marker_mask[i:i + 1], fp16_rounding=False, projections=proj)
+        rows += 1
+    dt = time.perf_counter() - t0
+    del limiter
+    return rows / dt, rows, dt, cpu_threads()
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return 0
+    from oracle import reference_forward as rf
+    from gliner_decide_metal_b200 import synthetic
+    threads = cpu_threads()
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=threads)
+    except Exception:
+        pass
+    w = synthetic.make_weights(seed=0, num_layers=LAYERS)
+    W = rf.OracleWeights(w, rf.OracleConfig())
+    proj = rf.relative_projections(W, fp16_rounding=False)
+    batch = synthetic.config2(seed=3)
+    rows_per_step = 1
+
+    def step(i):
+        r = i % BATCH
+        rf.forward(W, batch.input_ids[r:r + 1], batch.attention_mask[r:r + 1], batch.marker_indices[r:r + 1],
+                   batch.marker_mask[r:r + 1], fp16_rounding=False, projections=proj)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    dt = time.perf_counter() - t0
+    value = rows_per_step * args.steps / dt
+    sample = (f"{rows_per_step} row of the b32 L256 batch per step (one full 24-layer forward at L=256), "
+              f"{args.steps} steps")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "BASELINE config 2: DeBERTa-v3-large + GLiNER MLP, B=32, L=256 bucket",
+                       "batch": BATCH, "seq_len": SEQ, "rows_per_step": rows_per_step},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "CPU restatement (oracle/reference_forward.py, numpy fp32 BLAS) of DeBERTa.swift's forward; "
+                    "the reference's Swift/MLX code needs macOS + Apple silicon and cannot run on this host"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, devices):
+        self.devices = devices
+        self.proc = None
+        self.path = Path(tempfile.gettempdir()) / f"gdc_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                if int(parts[0]) not in self.devices:
+                    continue
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- native arm
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    import gliner_decide_metal_b200 as g
+    from gliner_decide_metal_b200 import synthetic
+
+    wpath = weights_path(rank, world, dist, args.weights)
+    model = g.GLiNERDecideClassifier(wpath, device=local)
+    stream = torch.cuda.ExternalStream(model.stream, device=torch.device("cuda", local))
+
+    # HBM-resident inputs: N_RESIDENT_BATCHES distinct batches per rank.
+    batches = [synthetic.config2(seed=1000 * rank + 3 + i) for i in range(N_RESIDENT_BATCHES)]
+    dev = []
+    for b in batches:
+        dev.append(dict(
+            ids=torch.from_numpy(b.input_ids.astype(np.int32)).cuda(local),
+            mask=torch.from_numpy(b.attention_mask.astype(np.float16)).cuda(local),
+            mi=torch.from_numpy(b.marker_indices.astype(np.int32)).cuda(local),
+            mm=torch.from_numpy(b.marker_mask.astype(np.float32)).cuda(local)))
+    hm, o = batches[0].marker_indices.shape[1:]
+    logits = torch.empty((BATCH, hm, o), dtype=torch.float32, device=f"cuda:{local}")
+    torch.cuda.synchronize(local)
+
+    def step(i):
+        d = dev[i % N_RESIDENT_BATCHES]
+        model.classify_device(BATCH, SEQ, hm, o, d["ids"].data_ptr(), d["mask"].data_ptr(), d["mi"].data_ptr(),
+                              d["mm"].data_ptr(), logits.data_ptr())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    model.check_errors()
+
+    # ---- timed region (device): kernel-group events recorded between launches
+    clocks = ClockSampler(list(range(torch.cuda.device_count())) if world > 1 else [local])
+    model.profile_reset()
+    model.profile_enable(True)
+    barrier()
+    torch.cuda.synchronize(local)
+    clocks.start()
+    time.sleep(0.4)  # let the sampler start before the load
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize(local)
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    barrier()
+    model.profile_enable(False)
+    prof = model.profile_read()
+    model.check_errors()
+    ms_max = max_over_ranks(ms)
+    seqs = BATCH * args.steps * world
+    value = seqs / (ms_max / 1e3)
+
+    # ---- e2e through the public API with host buffers
+    host_inputs = [g.DecisionInput(b.input_ids, b.attention_mask, b.marker_indices, b.marker_mask) for b in batches]
+    for i in range(2):
+        model.classify(host_inputs[i % N_RESIDENT_BATCHES])
+    barrier()
+    torch.cuda.synchronize(local)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        model.classify(host_inputs[i % N_RESIDENT_BATCHES])
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_value = seqs / e2e_s
+    R = BATCH * hm * o
+    h2d = BATCH * SEQ * (4 + 2) + R * (4 + 4)   # int32 ids, fp16 mask, int32 markers, fp32 marker mask
+    d2h = R * (4 + 2)                            # fp32 + fp16 logits
+
+    # ---- roofline of the dominant kernel (tcgen05 projection GEMMs)
+    peaks = measured_peaks()
+    gemm_names = ("qkv_gemm", "out_gemm", "ffn_up_gemm", "ffn_down_gemm")
+    gemm_ns = sum(prof.get(n, (0, 0))[0] for n in gemm_names)
+    gemm_launches = sum(prof.get(n, (0, 0))[1] for n in gemm_names)
+    gemm_flops = GEMM_FLOPS_PER_TOKEN * BATCH * SEQ * args.steps
+    achieved_tflops = gemm_flops / (gemm_ns * 1e-9) / 1e12 if gemm_ns else None
+    kernel_share = {k: round(v[0] / max(1, sum(x[0] for x in prof.values())), 4) for k, v in prof.items()}
+    kernel_ms_per_step = {k: round(v[0] / 1e6 / args.steps, 4) for k, v in prof.items()}
+    traffic = None
+    tpath = ROOT / "profiles" / "gemm_traffic.json"
+    if tpath.exists():
+        try:
+            traffic = json.loads(tpath.read_text()).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+    roofline = {"kernel": "gemm_tn_kernel (QKV / out / FFN-up / FFN-down projections)", "bound": "tensor",
+                "achieved": achieved_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": (achieved_tflops / peaks["bf16_tflops_sustained"]) if achieved_tflops else None,
+                "peak_source": f"{peaks['source']} bf16_tflops_sustained (kernel timed inside a long step)",
+                "traffic": traffic, "launches": gemm_launches,
+                "flops_per_launch_avg": gemm_flops / max(1, gemm_launches),
+                "kernel_ms_per_step": kernel_ms_per_step, "kernel_share": kernel_share}
+    attn_ns = prof.get("attention", (0, 0))[0]
+    if attn_ns:
+        roofline["attention_tflops"] = ATTN_FLOPS_PER_SEQ * BATCH * args.steps / (attn_ns * 1e-9) / 1e12
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, rows, dt, thr = cpu_reference_sample(args.cpu_seconds)
+        cpu = {"value": v, "unit": UNIT, "cores": thr, "kind": "port",
+               "sample": f"{rows} rows of the b32 L256 batch, one 24-layer fp32 forward per row, {dt:.1f} s "
+                         "(oracle/reference_forward.py, numpy BLAS)"}
+
+    launches_per_step = 1 + LAYERS * 7 + 3
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "config": {"workload": "BASELINE config 2: DeBERTa-v3-large (24 layers) + GLiNER MLP, B=32, "
+                                       "L=256 bucket, text lengths U[40,230], 1 task x 5 labels, random-init "
+                                       "N(0,0.02) fp16 weights",
+                           "batch_per_gpu": BATCH, "seq_len": SEQ, "parallelism": f"rows x{world} (no collective)",
+                           "resident_batches": N_RESIDENT_BATCHES,
+                           "l2": "no flush: each step streams 0.87 GB of weights (> 126 MB L2) and cycles "
+                                 f"{N_RESIDENT_BATCHES} distinct input batches"},
+                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "api": "gdc_classify (host numpy int64 ids / fp16 mask / int64 markers / fp32 marker mask)"},
+                "gpu_launches": launches_per_step * args.steps,
+                "roofline": roofline, "cpu_baseline": cpu, "clocks": clk}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -73,6 +73,7 @@ SIGNATURES = [
     ("gdc_relative_index_table", C.c_int, [_i32, _i32, _pi32]),
     ("gdc_residual_layer_norm", C.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _f32, _vp]),
     ("gdc_disentangled_attention", C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    ("gdc_disentangled_attention_scalar", C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     ("gdc_linear", C.c_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i64, _i32, _vp]),
     ("gdc_kernels_check_errors", C.c_int, []),
     ("gdc_last_error", C.c_char_p, []),
@@ -84,7 +85,7 @@ SIGNATURES = [
 def load():
     if not LIB_PATH.exists():
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m gliner_decide_metal_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python gliner_decide_metal_b200/build.py` "
             "(there is no CPU fallback)")
     lib = C.CDLL(str(LIB_PATH))
     for name, res, args in SIGNATURES:

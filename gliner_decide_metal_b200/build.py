@@ -3,7 +3,8 @@
 Compiles every ``csrc`` translation unit with nvcc for ``-gencode
 arch=compute_100a,code=sm_100a`` (objects under ``_build/``) and links the shared
 library in-tree next to this file, so it travels with the repository to the GPU host.
-Usage: ``python -m gliner_decide_metal_b200.build [--force] [-j N]``.
+Usage: ``python gliner_decide_metal_b200/build.py [--force] [-j N]`` (a plain script: it does
+not import the package, whose import loads the library this script builds).
 """
 from __future__ import annotations
 
@@ -48,8 +49,9 @@ def _compile(src: Path, force: bool, extra):
     cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *extra, "-c", str(src), "-o", str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
-        return obj, f"$ {' '.join(cmd)}\n{r.stdout}\n{r.stderr}"
-    return obj, (r.stderr if "warning" in r.stderr.lower() else None)
+        obj.unlink(missing_ok=True)
+        return obj, f"ERROR $ {' '.join(cmd)}\n{r.stdout}\n{r.stderr}"
+    return obj, (r.stderr if ("warning" in r.stderr.lower() or extra) else None)
 
 
 def build(force: bool = False, jobs: int | None = None, verbose_ptxas: bool = False) -> Path:
@@ -62,7 +64,7 @@ def build(force: bool = False, jobs: int | None = None, verbose_ptxas: bool = Fa
         for obj, msg in ex.map(lambda s: _compile(s, force, extra), srcs):
             objs.append(obj)
             if msg:
-                if "error" in msg.lower() and not obj.exists():
+                if msg.startswith("ERROR"):
                     errors.append(msg)
                 else:
                     print(msg, file=sys.stderr)

@@ -538,34 +538,62 @@ gdc_status gdc_residual_layer_norm(const uint16_t* x, const uint16_t* residual, 
                                     reinterpret_cast<__half*>(out), rows, cols, eps, static_cast<cudaStream_t>(stream));
 }
 
-gdc_status gdc_disentangled_attention(const uint16_t* qkv, const uint16_t* pos_qk, const uint16_t* key_mask,
-                                      uint16_t* ctx, int32_t batch, int32_t seq_len, int32_t heads, void* stream) {
-  clear_error();
-  if (!qkv || !pos_qk || !key_mask || !ctx) return set_error(GDC_ERR_NULL_POINTER, "gdc_disentangled_attention: null");
-  if (heads != 16) return set_error(GDC_ERR_UNSUPPORTED, "heads must be 16 (hidden 1024)");
-  if (batch <= 0 || seq_len <= 0 || seq_len > 512)
-    return set_error(GDC_ERR_INVALID_INPUT, "attention: batch > 0 and seq_len in [1, 512] required");
-  int* err = nullptr;
-  GDC_TRY(device_error_word(&err));
-  // relative table on the device: cached per device alongside the error word
+namespace {
+
+// Relative index table on the current device for the kernel-level entry points.
+gdc_status device_rel_table(int32_t** out) {
   static std::mutex mu;
   static int32_t* tables[64] = {};
   int dev = 0;
   GDC_CUDA_TRY(cudaGetDevice(&dev));
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!tables[dev]) {
-      int32_t host[1023];
-      build_relative_table(256, 512, host);
-      int32_t* d = nullptr;
-      GDC_CUDA_TRY(cudaMalloc(&d, sizeof(host)));
-      GDC_CUDA_TRY(cudaMemcpy(d, host, sizeof(host), cudaMemcpyHostToDevice));
-      tables[dev] = d;
-    }
+  if (dev < 0 || dev >= 64) return set_error(GDC_ERR_CUDA, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!tables[dev]) {
+    int32_t host[1023];
+    build_relative_table(256, 512, host);
+    int32_t* d = nullptr;
+    GDC_CUDA_TRY(cudaMalloc(&d, sizeof(host)));
+    GDC_CUDA_TRY(cudaMemcpy(d, host, sizeof(host), cudaMemcpyHostToDevice));
+    tables[dev] = d;
   }
+  *out = tables[dev];
+  return GDC_OK;
+}
+
+gdc_status check_attention_args(const uint16_t* qkv, const uint16_t* pos_qk, const uint16_t* key_mask,
+                                 const uint16_t* ctx, int32_t batch, int32_t seq_len, int32_t heads) {
+  if (!qkv || !pos_qk || !key_mask || !ctx) return set_error(GDC_ERR_NULL_POINTER, "attention: null argument");
+  if (heads != 16) return set_error(GDC_ERR_UNSUPPORTED, "heads must be 16 (hidden 1024)");
+  if (batch <= 0 || seq_len <= 0 || seq_len > 512)
+    return set_error(GDC_ERR_INVALID_INPUT, "attention: batch > 0 and seq_len in [1, 512] required");
+  return GDC_OK;
+}
+
+}  // namespace
+
+gdc_status gdc_disentangled_attention(const uint16_t* qkv, const uint16_t* pos_qk, const uint16_t* key_mask,
+                                      uint16_t* ctx, int32_t batch, int32_t seq_len, int32_t heads, void* stream) {
+  clear_error();
+  GDC_TRY(check_attention_args(qkv, pos_qk, key_mask, ctx, batch, seq_len, heads));
+  int* err = nullptr;
+  int32_t* table = nullptr;
+  GDC_TRY(device_error_word(&err));
+  GDC_TRY(device_rel_table(&table));
   return launch_attention(reinterpret_cast<const __half*>(qkv), reinterpret_cast<const __half*>(pos_qk),
-                          reinterpret_cast<const __half*>(key_mask), tables[dev], reinterpret_cast<__half*>(ctx), batch,
+                          reinterpret_cast<const __half*>(key_mask), table, reinterpret_cast<__half*>(ctx), batch,
                           seq_len, heads, static_cast<cudaStream_t>(stream), err);
+}
+
+gdc_status gdc_disentangled_attention_scalar(const uint16_t* qkv, const uint16_t* pos_qk, const uint16_t* key_mask,
+                                             uint16_t* ctx, int32_t batch, int32_t seq_len, int32_t heads,
+                                             void* stream) {
+  clear_error();
+  GDC_TRY(check_attention_args(qkv, pos_qk, key_mask, ctx, batch, seq_len, heads));
+  int32_t* table = nullptr;
+  GDC_TRY(device_rel_table(&table));
+  return launch_attention_simt(reinterpret_cast<const __half*>(qkv), reinterpret_cast<const __half*>(pos_qk),
+                               reinterpret_cast<const __half*>(key_mask), table, reinterpret_cast<__half*>(ctx), batch,
+                               seq_len, heads, static_cast<cudaStream_t>(stream));
 }
 
 gdc_status gdc_linear(const uint16_t* a, const uint16_t* w, const uint16_t* bias, uint16_t* out, int64_t M, int32_t N,

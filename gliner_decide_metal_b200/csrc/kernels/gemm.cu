@@ -241,36 +241,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ host side
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// 2-D fp16 tensor map: `rows` x `cols` (cols contiguous), row pitch `ld` elements,
-// box = box_rows x 64 columns, 128-byte swizzle, out-of-bounds rows read as zero.
-gdc_status make_tmap(CUtensorMap* map, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld,
-                     uint32_t box_rows) {
-  auto fn = get_encode_fn();
-  if (!fn) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {ld * sizeof(__half)};
-  cuuint32_t box[2] = {64, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
-  return GDC_OK;
-}
-
 template <int BN, int ACT>
 gdc_status launch_gemm_variant(const CUtensorMap& ta, const CUtensorMap& tw, const __half* bias, __half* out,
                                long long ldo, int M, int N, int K, cudaStream_t stream, int* err) {
@@ -291,6 +261,37 @@ gdc_status launch_gemm_variant(const CUtensorMap& ta, const CUtensorMap& tw, con
 }
 
 }  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D fp16 tensor map: `rows` x `cols` (cols contiguous), row pitch `ld` elements,
+// box = box_rows x 64 columns, 128-byte swizzle, out-of-bounds rows read as zero.
+gdc_status make_tmap_2d(void* map_out, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                        uint32_t box_rows) {
+  CUtensorMap* map = static_cast<CUtensorMap*>(map_out);
+  auto fn = get_encode_fn();
+  if (!fn) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * sizeof(__half)};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return GDC_OK;
+}
 
 int device_sm_count(int device) {
   static int counts[64] = {};
@@ -315,8 +316,8 @@ gdc_status launch_linear(const __half* a, int64_t lda, const __half* w, const __
   if (act < 0 || act > 2) return set_error(GDC_ERR_INVALID_INPUT, "linear: unknown activation %d", act);
   const int bn = (N % 256 == 0) ? 256 : 128;
   CUtensorMap ta, tw;
-  GDC_TRY(make_tmap(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), kBM));
-  GDC_TRY(make_tmap(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn)));
+  GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), kBM));
+  GDC_TRY(make_tmap_2d(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn)));
   const int m = int(M);
   if (bn == 256) {
     if (act == kActGelu) return launch_gemm_variant<256, kActGelu>(ta, tw, bias, out, ldo, m, N, K, stream, err);

@@ -53,4 +53,10 @@ gdc_status launch_decode(const float* logits, int batch, int max_heads, int max_
 
 int device_sm_count(int device);
 
+// 2-D fp16 TMA descriptor: `rows` x `cols` (cols contiguous), row pitch `ld` elements,
+// box = box_rows x 64 columns, 128-byte swizzle, out-of-bounds rows read as zero.
+// (CUtensorMap is passed as void* to keep <cuda.h> out of this header.)
+gdc_status make_tmap_2d(void* map, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                        uint32_t box_rows);
+
 }  // namespace gdc

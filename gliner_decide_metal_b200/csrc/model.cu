@@ -120,22 +120,22 @@ gdc_status model_load(const char* path, const gdc_config* cfg_in, int device, gd
   m->classifier_hidden = int(DC);
 
   do {
-    if ((st = get("encoder.embeddings.word_embeddings.weight", {cfg.vocab_size, E}, &m->word_emb))) break;
-    if ((st = get("encoder.embeddings.LayerNorm.weight", {E}, &m->emb_ln_g))) break;
-    if ((st = get("encoder.embeddings.LayerNorm.bias", {E}, &m->emb_ln_b))) break;
-    if ((st = get("encoder.encoder.rel_embeddings.weight", {512, E}, &m->rel_ln))) break;
+    if ((st = get("encoder.embeddings.word_embeddings.weight", {cfg.vocab_size, E}, &m->word_emb)) != GDC_OK) break;
+    if ((st = get("encoder.embeddings.LayerNorm.weight", {E}, &m->emb_ln_g)) != GDC_OK) break;
+    if ((st = get("encoder.embeddings.LayerNorm.bias", {E}, &m->emb_ln_b)) != GDC_OK) break;
+    if ((st = get("encoder.encoder.rel_embeddings.weight", {512, E}, &m->rel_ln)) != GDC_OK) break;
     for (int i = 0; i < cfg.num_hidden_layers && st == GDC_OK; ++i) {
       const std::string p = "encoder.encoder.layer." + std::to_string(i);
       LayerWeights& L = m->layers[size_t(i)];
       // q, k, v are concatenated into one [3E, E] matrix below.
       std::vector<uint16_t> wq, wk, wv, bq, bk, bv;
       std::vector<int64_t> sw = {E, E}, sb = {E};
-      if ((st = file.get_f16(p + ".attention.self.query_proj.weight", &sw, &wq))) break;
-      if ((st = file.get_f16(p + ".attention.self.key_proj.weight", &sw, &wk))) break;
-      if ((st = file.get_f16(p + ".attention.self.value_proj.weight", &sw, &wv))) break;
-      if ((st = file.get_f16(p + ".attention.self.query_proj.bias", &sb, &bq))) break;
-      if ((st = file.get_f16(p + ".attention.self.key_proj.bias", &sb, &bk))) break;
-      if ((st = file.get_f16(p + ".attention.self.value_proj.bias", &sb, &bv))) break;
+      if ((st = file.get_f16(p + ".attention.self.query_proj.weight", &sw, &wq)) != GDC_OK) break;
+      if ((st = file.get_f16(p + ".attention.self.key_proj.weight", &sw, &wk)) != GDC_OK) break;
+      if ((st = file.get_f16(p + ".attention.self.value_proj.weight", &sw, &wv)) != GDC_OK) break;
+      if ((st = file.get_f16(p + ".attention.self.query_proj.bias", &sb, &bq)) != GDC_OK) break;
+      if ((st = file.get_f16(p + ".attention.self.key_proj.bias", &sb, &bk)) != GDC_OK) break;
+      if ((st = file.get_f16(p + ".attention.self.value_proj.bias", &sb, &bv)) != GDC_OK) break;
       PendingUpload uw, ub;
       uw.dst = &L.wqkv;
       uw.host.reserve(wq.size() * 3);
@@ -148,22 +148,22 @@ gdc_status model_load(const char* path, const gdc_config* cfg_in, int device, gd
       ub.host.insert(ub.host.end(), bv.begin(), bv.end());
       ups.push_back(std::move(uw));
       ups.push_back(std::move(ub));
-      if ((st = get(p + ".attention.output.dense.weight", {E, E}, &L.wo))) break;
-      if ((st = get(p + ".attention.output.dense.bias", {E}, &L.bo))) break;
-      if ((st = get(p + ".attention.output.LayerNorm.weight", {E}, &L.ln1_g))) break;
-      if ((st = get(p + ".attention.output.LayerNorm.bias", {E}, &L.ln1_b))) break;
-      if ((st = get(p + ".intermediate.dense.weight", {F, E}, &L.w1))) break;
-      if ((st = get(p + ".intermediate.dense.bias", {F}, &L.b1))) break;
-      if ((st = get(p + ".output.dense.weight", {E, F}, &L.w2))) break;
-      if ((st = get(p + ".output.dense.bias", {E}, &L.b2))) break;
-      if ((st = get(p + ".output.LayerNorm.weight", {E}, &L.ln2_g))) break;
-      if ((st = get(p + ".output.LayerNorm.bias", {E}, &L.ln2_b))) break;
+      if ((st = get(p + ".attention.output.dense.weight", {E, E}, &L.wo)) != GDC_OK) break;
+      if ((st = get(p + ".attention.output.dense.bias", {E}, &L.bo)) != GDC_OK) break;
+      if ((st = get(p + ".attention.output.LayerNorm.weight", {E}, &L.ln1_g)) != GDC_OK) break;
+      if ((st = get(p + ".attention.output.LayerNorm.bias", {E}, &L.ln1_b)) != GDC_OK) break;
+      if ((st = get(p + ".intermediate.dense.weight", {F, E}, &L.w1)) != GDC_OK) break;
+      if ((st = get(p + ".intermediate.dense.bias", {F}, &L.b1)) != GDC_OK) break;
+      if ((st = get(p + ".output.dense.weight", {E, F}, &L.w2)) != GDC_OK) break;
+      if ((st = get(p + ".output.dense.bias", {E}, &L.b2)) != GDC_OK) break;
+      if ((st = get(p + ".output.LayerNorm.weight", {E}, &L.ln2_g)) != GDC_OK) break;
+      if ((st = get(p + ".output.LayerNorm.bias", {E}, &L.ln2_b)) != GDC_OK) break;
     }
     if (st) break;
-    if ((st = get("classifier.0.weight", {DC, E}, &m->cls_w0))) break;
-    if ((st = get("classifier.0.bias", {DC}, &m->cls_b0))) break;
-    if ((st = get("classifier.2.weight", {1, DC}, &m->cls_w2))) break;
-    if ((st = get("classifier.2.bias", {1}, &m->cls_b2))) break;
+    if ((st = get("classifier.0.weight", {DC, E}, &m->cls_w0)) != GDC_OK) break;
+    if ((st = get("classifier.0.bias", {DC}, &m->cls_b0)) != GDC_OK) break;
+    if ((st = get("classifier.2.weight", {1, DC}, &m->cls_w2)) != GDC_OK) break;
+    if ((st = get("classifier.2.bias", {1}, &m->cls_b2)) != GDC_OK) break;
   } while (false);
   // LN(rel) scratch: the encoder LN params are needed only at load.
   std::vector<uint16_t> rel_g, rel_b;

@@ -259,6 +259,14 @@ gdc_status gdc_disentangled_attention(const uint16_t* qkv, const uint16_t* pos_q
                                       const uint16_t* key_mask, uint16_t* ctx, int32_t batch,
                                       int32_t seq_len, int32_t heads, void* stream);
 
+/* Same contract as gdc_disentangled_attention, computed by a CUDA-core kernel with one
+ * warp per query row (the structure of FusedKernels.swift:13-81). Used to cross-check
+ * the tensor-core kernel on the device at sizes the CPU oracle cannot reach; the forward
+ * does not use it. */
+gdc_status gdc_disentangled_attention_scalar(const uint16_t* qkv, const uint16_t* pos_qk,
+                                             const uint16_t* key_mask, uint16_t* ctx, int32_t batch,
+                                             int32_t seq_len, int32_t heads, void* stream);
+
 /* addMM(bias, x, W^T) (DeBERTa.swift:69-71, 89-91) on tcgen05 tensor cores:
  * out[M,N] = act(a[M,K] . w[N,K]^T + bias[N]) in fp16 with fp32 accumulation;
  * act: 0 = none, 1 = exact-erf GELU, 2 = ReLU. N must be a multiple of 256 and K a

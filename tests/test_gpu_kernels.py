@@ -217,3 +217,24 @@ def test_attention_masked_keys_get_zero_weight():
         outs.append(_host(ctx))
     torch.cuda.synchronize()
     assert np.array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("B,L", [(32, 256), (4, 512), (8, 64), (3, 200)])
+def test_attention_tensor_core_matches_scalar_kernel(B, L):
+    """Full BASELINE config-1 shape (B=32, H=16, L=256, key lengths U[64, 256]) and L=512:
+    the tcgen05 kernel against the CUDA-core kernel on the device (the CPU oracle is too
+    slow at this size)."""
+    torch = _torch()
+    rng = np.random.Generator(np.random.PCG64(L + B))
+    lengths = rng.integers(min(64, L), L + 1, B)
+    qkv, pos, mask = _attention_case(B, L, seed=77 + L, lengths=lengths)
+    pq, pp, pm = _ptr(qkv), _ptr(pos), _ptr(mask)
+    a = torch.empty((B * L, 1024), dtype=torch.float16, device="cuda")
+    b = torch.empty((B * L, 1024), dtype=torch.float16, device="cuda")
+    _check(_lib().gdc_disentangled_attention(pq, pp, pm, a.data_ptr(), B, L, 16, None))
+    _check(_lib().gdc_disentangled_attention_scalar(pq, pp, pm, b.data_ptr(), B, L, 16, None))
+    torch.cuda.synchronize()
+    _check(_lib().gdc_kernels_check_errors())
+    x, y = _host(a).astype(np.float32), _host(b).astype(np.float32)
+    assert np.isfinite(x).all()
+    np.testing.assert_allclose(x, y, rtol=1e-2, atol=4e-3)
