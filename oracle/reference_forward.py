@@ -83,7 +83,8 @@ def relative_bucket(relative: np.ndarray, position_buckets: int = 256,
     abs_pos = np.where((r > -mid) & (r < mid), mid - 1, np.abs(r)).astype(np.int64)
     log_pos = np.ceil(
         np.log(abs_pos.astype(np.float64) / float(mid))
-        / math.log(float(max_relative_positions - 1) / float(mid))
+        / np.log(np.float64(max_relative_positions - 1) / float(mid))  # same log() as the numerator:
+        # at |r| = 511 the ratio is then exactly 1 and ceil(127.0) = 127, as in Swift
         * float(mid - 1)
     ).astype(np.int64) + mid
     sign = np.where(r < 0, -1, 1)
