@@ -44,10 +44,12 @@ gdc_status launch_attention(const __half* qkv, const __half* pos_qk, const __hal
     if (e != cudaSuccess) return set_error(GDC_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  dim3 grid((seq_len + attn::kTile - 1) / attn::kTile, heads, batch);
-  if (batch > 65535) return set_error(GDC_ERR_UNSUPPORTED, "attention: batch %d > 65535", batch);
+  const long long items = (long long)((seq_len + attn::kTile - 1) / attn::kTile) * heads * batch;
+  if (items > (1ll << 30)) return set_error(GDC_ERR_UNSUPPORTED, "attention: too many work items");
+  const int sms = device_sm_count(dev);
+  const int grid = items < sms ? int(items) : sms;  // persistent: one CTA per SM
   attn::attention_tc_kernel<<<grid, attn::kThreads, attn::kSmemBytes, stream>>>(tm_qkv, tm_pos, key_mask, rel_table,
-                                                                                ctx, seq_len, heads, err);
+                                                                                ctx, batch, seq_len, heads, err);
   return check_launch("attention_tc_kernel");
 }
 

@@ -10,8 +10,8 @@
 //   warp 1      allocates 2*BN TMEM columns; lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
 //               into one of two TMEM accumulators and commits to the ring's empty barriers
 //               and, per tile, to the accumulator-full barrier.
-//   warps 2-9   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
-//               32*(w%4)..+32, two warps per lane quarter split the columns), add bias,
+//   warps 2-17  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+32, four warps per lane quarter split the columns), add bias,
 //               apply GELU / ReLU, round to fp16, store 16-byte vectors; then release the
 //               accumulator so the MMA warp can start the tile after next.
 // Every mbarrier wait is bounded (ptx::mbar_wait); on a timeout the kernel flags the error
@@ -19,6 +19,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "kernels.h"
@@ -29,7 +30,8 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 320;
+constexpr int kEpiWarps = 16;                  // 4 per TMEM lane quarter, each 1/4 of the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 template <int BN>
 struct GemmShape {
@@ -41,7 +43,21 @@ struct GemmShape {
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
 };
 
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26
+// (|error| <= 1.5e-7): erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2),
+// t = 1 / (1 + p x), x >= 0; odd extension for x < 0. The error is far below the fp16
+// rounding of the GEMM output.
+__device__ __forceinline__ float erf_as7126(float x) {
+  const float ax = fabsf(x);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
+  float poly = fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t,
+                    0.254829592f) * t;
+  const float y = 1.0f - poly * __expf(-ax * ax);
+  return copysignf(y, x);
+}
+
+// Exact-erf GELU of MLXNN.gelu (DeBERTa.swift:421): 0.5 x (1 + erf(x / sqrt 2)).
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f)); }
 
 template <int BN, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -73,7 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull[a], 1);
-      ptx::mbar_init(&tempty[a], 8);
+      ptx::mbar_init(&tempty[a], kEpiWarps);
     }
     ptx::mbar_init(drain, 1);
     ptx::fence_barrier_init();
@@ -177,9 +193,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2..9.
-    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
-    const int col_half = (warp - 2) >> 2;   // which half of the BN columns
+    // Epilogue warps 2..(2 + kEpiWarps): warp w reads TMEM lane quarter w % 4 and the
+    // column group (w - 2) / 4 (BN / 4 columns, two 32-column chunks in flight per wait).
+    const int quarter = warp & 3;
+    const int group = (warp - 2) >> 2;
+    constexpr int kGroupCols = BN / 4;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -191,38 +209,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = mb * kBM + quarter * 32 + lane;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 2; c += 32) {
-        const int col = col_half * (BN / 2) + c;
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(t_row + uint32_t(col), r);
+      for (int c = 0; c < kGroupCols; c += 64) {
+        const int col = group * kGroupCols + c;
+        uint32_t r[2][32];
+        ptx::tmem_ld_32x32b_x32(t_row + uint32_t(col), r[0]);
+        if (kGroupCols >= 64) ptx::tmem_ld_32x32b_x32(t_row + uint32_t(col + 32), r[1]);
         ptx::tmem_wait_ld();
-        const int n0 = nb * BN + col;
-        const uint4* bsrc = reinterpret_cast<const uint4*>(bias + n0);
-        uint32_t packed[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 bv = __ldg(bsrc + q);
-          const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+        for (int half = 0; half < (kGroupCols >= 64 ? 2 : 1); ++half) {
+          const int n0 = nb * BN + col + half * 32;
+          const uint4* bsrc = reinterpret_cast<const uint4*>(bias + n0);
+          uint32_t packed[16];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 bf = __half22float2(bh[j]);
-            float v0 = __uint_as_float(r[q * 8 + 2 * j]) + bf.x;
-            float v1 = __uint_as_float(r[q * 8 + 2 * j + 1]) + bf.y;
-            if (ACT == kActGelu) {
-              v0 = gelu_erf(v0);
-              v1 = gelu_erf(v1);
-            } else if (ACT == kActRelu) {
-              v0 = fmaxf(v0, 0.f);
-              v1 = fmaxf(v1, 0.f);
+          for (int q = 0; q < 4; ++q) {
+            const uint4 bv = __ldg(bsrc + q);
+            const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 bf = __half22float2(bh[j]);
+              float v0 = __uint_as_float(r[half][q * 8 + 2 * j]) + bf.x;
+              float v1 = __uint_as_float(r[half][q * 8 + 2 * j + 1]) + bf.y;
+              if (ACT == kActGelu) {
+                v0 = gelu_erf(v0);
+                v1 = gelu_erf(v1);
+              } else if (ACT == kActRelu) {
+                v0 = fmaxf(v0, 0.f);
+                v1 = fmaxf(v1, 0.f);
+              }
+              packed[q * 4 + j] = ptx::pack_half2(v0, v1);
             }
-            packed[q * 4 + j] = ptx::pack_half2(v0, v1);
           }
-        }
-        if (row < M) {
-          uint4* dst = reinterpret_cast<uint4*>(out + (long long)row * ldo + n0);
+          if (row < M) {
+            uint4* dst = reinterpret_cast<uint4*>(out + (long long)row * ldo + n0);
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(packed[q * 4], packed[q * 4 + 1], packed[q * 4 + 2], packed[q * 4 + 3]);
+            for (int q = 0; q < 4; ++q)
+              dst[q] = make_uint4(packed[q * 4], packed[q * 4 + 1], packed[q * 4 + 2], packed[q * 4 + 3]);
+          }
         }
       }
       ptx::tc_fence_before();
@@ -314,6 +336,13 @@ gdc_status launch_linear(const __half* a, int64_t lda, const __half* w, const __
       (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(bias) & 15))
     return set_error(GDC_ERR_INVALID_INPUT, "linear: pointers must be 16-byte aligned and strides multiples of 8");
   if (act < 0 || act > 2) return set_error(GDC_ERR_INVALID_INPUT, "linear: unknown activation %d", act);
+  // Large M runs on CTA pairs (gemm_pair.cu); GDC_GEMM_SINGLE_CTA=1 selects this kernel for
+  // every M (used by tests to cross-check the two implementations).
+  static const bool force_single = [] {
+    const char* e = std::getenv("GDC_GEMM_SINGLE_CTA");
+    return e != nullptr && e[0] == '1';
+  }();
+  if (M > 128 && !force_single) return launch_linear_pair(a, lda, w, bias, out, ldo, M, N, K, act, stream, err);
   const int bn = (N % 256 == 0) ? 256 : 128;
   CUtensorMap ta, tw;
   GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), kBM));

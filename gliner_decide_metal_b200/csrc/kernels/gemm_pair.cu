@@ -1,0 +1,316 @@
+// Pair-CTA (cta_group::2) tcgen05 GEMM: out = act(A . W^T + bias) with 256-row tiles.
+//
+// Same contract as gemm_tn_kernel (gemm.cu) for the encoder projections
+// (DeBERTa.swift:60-92, 420-427). A single CTA issuing M=128 x N=256 MMAs needs more
+// shared-memory bandwidth than an SM has (TMA writes plus MMA reads of A and B), so
+// large-M GEMMs run on CTA pairs (a cluster of 2 on neighbouring SMs):
+//   * each CTA TMA-loads its own 128 rows of the A tile and its own BN/2 rows of the W
+//     tile into identical shared-memory offsets; completion of both CTAs' loads is
+//     signalled on the leader CTA's "full" barrier (cp.async.bulk.tensor .cta_group::2);
+//   * the leader issues tcgen05.mma.cta_group::2 (M=256, N=BN, K=16): each CTA's tensor
+//     core produces its 128 rows x BN columns in its own TMEM, B is shared across the pair;
+//   * the leader's commits arrive on both CTAs' "empty" (ring slot free) and "tmem full"
+//     barriers; both CTAs' epilogues arrive on the leader's "tmem empty" barrier.
+// Persistent over tiles (one tile sequence per pair), 2 TMEM accumulators so the
+// epilogue of one tile overlaps the main loop of the next. All waits are bounded.
+#include <cuda.h>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace gdc {
+namespace {
+
+constexpr int kBK = 64;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+
+template <int BN>
+struct PairShape {
+  static constexpr int kABytes = 128 * kBK * 2;        // this CTA's 128 rows of A
+  static constexpr int kBBytes = (BN / 2) * kBK * 2;   // this CTA's BN/2 rows of W
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (200 * 1024) / kStageBytes;
+  static constexpr int kTmemCols = (2 * BN <= 256) ? 256 : 512;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+// erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26
+// (|error| <= 1.5e-7): erf(x) = 1 - (a1 t + ... + a5 t^5) exp(-x^2), t = 1 / (1 + p x).
+__device__ __forceinline__ float erf_as7126(float x) {
+  const float ax = fabsf(x);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
+  const float poly =
+      fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t, 0.254829592f) * t;
+  return copysignf(1.0f - poly * __expf(-ax * ax), x);
+}
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f)); }
+
+template <int BN, int ACT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                     const __half* __restrict__ bias, __half* __restrict__ out, int M, int N, int K, long long ldo,
+                     int* err) {
+  using S = PairShape<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + S::kStages * S::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_b + S::kStages * S::kBBytes);
+  uint64_t* empty = full + S::kStages;
+  uint64_t* tfull = empty + S::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const bool leader = rank == 0;
+  const int num_m = (M + 255) / 256;
+  const int num_tiles = num_m * (N / BN);
+  const int kblocks = K / kBK;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::kStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&tfull[a], 1);
+      ptx::mbar_init(&tempty[a], 2 * kEpiWarps);
+    }
+    ptx::mbar_init(drain, 1);
+    ptx::fence_barrier_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc_pair(tmem_slot, S::kTmemCols);
+    ptx::tmem_relinquish_pair();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA signal
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      ptx::prefetch_tensor_map(&tm_a);
+      ptx::prefetch_tensor_map(&tm_w);
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        const int mb = tile % num_m;
+        const int nb = tile / num_m;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1u, err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t leader_full = ptx::mapa_shared(ptx::smem_u32(&full[stage]), 0);
+          if (leader) ptx::mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
+          ptx::tma_load_2d_pair(s_a + stage * S::kABytes, &tm_a, kb * kBK, mb * 256 + int(rank) * 128, leader_full);
+          ptx::tma_load_2d_pair(s_b + stage * S::kBBytes, &tm_w, kb * kBK, nb * BN + int(rank) * (BN / 2),
+                                leader_full);
+          ++issued;
+          if (++stage == S::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // The leader's MMAs read this CTA's ring slots; their "empty" arrivals mean the loads
+      // landed and were consumed. Wait (bounded) for the last issue of each slot.
+      const long long tail = issued < S::kStages ? issued : S::kStages;
+      for (long long j = 0; j < tail; ++j) {
+        int s = stage - 1 - int(j);
+        uint32_t ph = phase;
+        while (s < 0) {
+          s += S::kStages;
+          ph ^= 1u;
+        }
+        const unsigned long long t0 = ptx::globaltimer();
+        while (!ptx::mbar_try_wait(&empty[s], ph) && ptx::globaltimer() - t0 < ptx::kTimeoutNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = ptx::idesc_f16_f32(256, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!ptx::mbar_wait(&tempty[acc], aphase ^ 1u, err)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!ptx::mbar_wait(&full[stage], phase, err)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a_addr = ptx::smem_u32(s_a + stage * S::kABytes);
+          const uint32_t b_addr = ptx::smem_u32(s_b + stage * S::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            ptx::umma_f16_ss_pair(d_tmem, ptx::desc_kmajor_sw128(a_addr + k * 32),
+                                  ptx::desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+          const uint32_t e = ptx::smem_u32(&empty[stage]);
+          ptx::umma_commit_pair(ptx::mapa_shared(e, 0));
+          ptx::umma_commit_pair(ptx::mapa_shared(e, 1));
+          if (++stage == S::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        const uint32_t f = ptx::smem_u32(&tfull[acc]);
+        ptx::umma_commit_pair(ptx::mapa_shared(f, 0));
+        ptx::umma_commit_pair(ptx::mapa_shared(f, 1));
+      }
+      ptx::umma_commit_pair(ptx::mapa_shared(ptx::smem_u32(drain), 0));
+      const unsigned long long t0 = ptx::globaltimer();
+      while (!ptx::mbar_try_wait(drain, 0) && ptx::globaltimer() - t0 < ptx::kTimeoutNs) {
+      }
+    }
+  } else {
+    // Epilogue warps 2..(1 + kEpiWarps): TMEM lane quarter warp % 4, column half (warp-2)/4.
+    const int quarter = warp & 3;
+    const int col_half = (warp - 2) >> 2;
+    constexpr int kHalfCols = BN / 2;
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      if (!ptx::mbar_wait(&tfull[acc], aphase, err)) break;
+      ptx::tc_fence_after();
+      const int mb = tile % num_m;
+      const int nb = tile / num_m;
+      const int row = mb * 256 + int(rank) * 128 + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < kHalfCols; c += 32) {
+        const int col = col_half * kHalfCols + c;
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(t_row + uint32_t(col), r);
+        ptx::tmem_wait_ld();
+        const int n0 = nb * BN + col;
+        const uint4* bsrc = reinterpret_cast<const uint4*>(bias + n0);
+        uint32_t packed[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 bv = __ldg(bsrc + q);
+          const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 bf = __half22float2(bh[j]);
+            float v0 = __uint_as_float(r[q * 8 + 2 * j]) + bf.x;
+            float v1 = __uint_as_float(r[q * 8 + 2 * j + 1]) + bf.y;
+            if (ACT == kActGelu) {
+              v0 = gelu_erf(v0);
+              v1 = gelu_erf(v1);
+            } else if (ACT == kActRelu) {
+              v0 = fmaxf(v0, 0.f);
+              v1 = fmaxf(v1, 0.f);
+            }
+            packed[q * 4 + j] = ptx::pack_half2(v0, v1);
+          }
+        }
+        if (row < M) {
+          uint4* dst = reinterpret_cast<uint4*>(out + (long long)row * ldo + n0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(packed[q * 4], packed[q * 4 + 1], packed[q * 4 + 2], packed[q * 4 + 3]);
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&tempty[acc]), 0));
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::cluster_sync();  // neither CTA leaves while the pair may still touch its memory
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc_pair(tmem_base, S::kTmemCols);
+  }
+}
+
+template <int BN, int ACT>
+gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, const __half* bias, __half* out,
+                               long long ldo, int M, int N, int K, cudaStream_t stream, int* err) {
+  using S = PairShape<BN>;
+  auto kern = gemm_pair_kernel<BN, ACT>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return set_error(GDC_ERR_CUDA, "device ordinal out of range");
+  if (!configured[dev]) {
+    GDC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes));
+    configured[dev] = true;
+  }
+  const int num_tiles = ((M + 255) / 256) * (N / BN);
+  const int pairs_avail = device_sm_count(dev) / 2;
+  const int pairs = num_tiles < pairs_avail ? num_tiles : pairs_avail;
+  kern<<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(ta, tw, bias, out, M, N, K, ldo, err);
+  return check_launch("gemm_pair_kernel");
+}
+
+// Tile width giving the best last-wave occupancy over the available CTA pairs.
+int choose_bn(int64_t M, int N, int pairs) {
+  const int cands[3] = {256, 192, 128};
+  int best = 0;
+  double best_eff = -1.0;
+  for (int bn : cands) {
+    if (N % bn) continue;
+    const double tiles = double((M + 255) / 256) * (N / bn);
+    const double waves = double(int64_t((tiles + pairs - 1) / pairs));
+    const double eff = tiles / (waves * pairs) * (bn == 128 ? 0.9 : 1.0);  // narrow tiles cost more per FLOP
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+}  // namespace
+
+gdc_status launch_linear_pair(const __half* a, int64_t lda, const __half* w, const __half* bias, __half* out,
+                              int64_t ldo, int64_t M, int N, int K, int act, cudaStream_t stream, int* err) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int bn = choose_bn(M, N, device_sm_count(dev) / 2);
+  if (bn == 0) return set_error(GDC_ERR_UNSUPPORTED, "linear: N=%d is not a multiple of 128", N);
+  CUtensorMap ta, tw;
+  GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), 128));
+  GDC_TRY(make_tmap_2d(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 2)));
+  const int m = int(M);
+#define GDC_PAIR_CASE(BNV)                                                                              \
+  if (bn == BNV) {                                                                                      \
+    if (act == kActGelu) return launch_pair_variant<BNV, kActGelu>(ta, tw, bias, out, ldo, m, N, K, stream, err); \
+    if (act == kActRelu) return launch_pair_variant<BNV, kActRelu>(ta, tw, bias, out, ldo, m, N, K, stream, err); \
+    return launch_pair_variant<BNV, kActNone>(ta, tw, bias, out, ldo, m, N, K, stream, err);          \
+  }
+  GDC_PAIR_CASE(256)
+  GDC_PAIR_CASE(192)
+  GDC_PAIR_CASE(128)
+#undef GDC_PAIR_CASE
+  return set_error(GDC_ERR_UNSUPPORTED, "linear: no tile width for N=%d", N);
+}
+
+}  // namespace gdc

@@ -19,6 +19,11 @@ enum Act : int { kActNone = 0, kActGelu = 1, kActRelu = 2 };
 gdc_status launch_linear(const __half* a, int64_t lda, const __half* w, const __half* bias, __half* out,
                          int64_t ldo, int64_t M, int N, int K, int act, cudaStream_t stream, int* err);
 
+// Same contract on CTA pairs (cta_group::2, 256-row tiles); launch_linear dispatches here
+// for M > 128.
+gdc_status launch_linear_pair(const __half* a, int64_t lda, const __half* w, const __half* bias, __half* out,
+                              int64_t ldo, int64_t M, int N, int K, int act, cudaStream_t stream, int* err);
+
 // out = LN(x + residual) * gamma + beta (rows x cols, fp16; fp32 statistics). The
 // sum x + residual is rounded to fp16 first, as the reference's fp16 add does.
 // residual may be null. cols % 256 == 0, cols <= 4096.
