@@ -24,9 +24,9 @@
 //         (fp32), write fp16 probabilities as a K-major SW128 operand
 //   MMA   O_j = Prob . V (cols 384-447, V as an MN-major operand)
 //   rows  O = O * exp(m_old - m_new) + O_j in registers
-// Threads: 16 row warps; warp w owns TMEM lane quarter w % 4 (query rows / key rows
-// 32*(w%4)..+32) and part w / 4 of the columns / keys of every phase. Warp 16 lane 0
-// issues the MMAs; warp 17 issues the TMA loads (and scans key masks). Every wait is a
+// Threads: 4 * kParts row warps; warp w owns TMEM lane quarter w % 4 (query rows / key rows
+// 32*(w%4)..+32) and part w / 4 of the columns / keys of every phase. The next warp's lane 0
+// issues the MMAs; the last warp issues the TMA loads (and scans key masks). Every wait is a
 // bounded mbarrier wait; the row warps sleep in theirs.
 #pragma once
 
@@ -40,8 +40,14 @@ namespace attn {
 
 constexpr int kTile = 128;      // query rows per item and keys per tile
 constexpr int kWin = 256;       // relative-position window rows per pair
-constexpr int kParts = 4;       // row warps per TMEM lane quarter
+#ifndef GDC_ATTN_PARTS
+#define GDC_ATTN_PARTS 2
+#endif
+constexpr int kParts = GDC_ATTN_PARTS;   // row warps per TMEM lane quarter (2 or 4)
 constexpr int kRowWarps = 4 * kParts;
+constexpr int kColsPP = 256 / kParts;    // C / P columns drained per row warp
+constexpr int kKeysPP = 128 / kParts;    // keys scored per row warp
+constexpr int kOPP = 64 / kParts;        // O columns accumulated per row warp
 constexpr int kRowThreads = kRowWarps * 32;
 constexpr int kThreads = kRowThreads + 64;  // + MMA issuer warp + TMA producer warp
 constexpr int kTmemCols = 512;
@@ -90,10 +96,10 @@ struct RowSync {
   }
 };
 
-// 64 fp32 TMEM columns of this thread's lane -> fp16, 16-byte stores into the swizzled row.
+// kColsPP fp32 TMEM columns of this thread's lane -> fp16, 16-byte stores into the swizzled row.
 __device__ __forceinline__ void drain_rows_f16(uint32_t taddr, uint8_t* base, int row, int col0) {
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
+  for (int c = 0; c < kColsPP / 32; ++c) {
     uint32_t r[32];
     ptx::tmem_ld_32x32b_x32(taddr + uint32_t(c * 32), r);
     ptx::tmem_wait_ld();
@@ -108,6 +114,11 @@ __device__ __forceinline__ void drain_rows_f16(uint32_t taddr, uint8_t* base, in
     }
   }
 }
+
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { ptx::tmem_ld_32x32b_x32(taddr, r); }
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[16]) { ptx::tmem_ld_32x32b_x16(taddr, r); }
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[32]) { ptx::tmem_st_32x32b_x32(taddr, r); }
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[16]) { ptx::tmem_st_32x32b_x16(taddr, r); }
 
 // Work item decomposition: item = (b * heads + h) * n_qt + qt.
 struct Item {
@@ -139,10 +150,14 @@ __device__ __forceinline__ MaskChunk load_mask_chunk(const __half* key_mask, lon
     if (k + 8 <= L && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
       c.v[h] = __ldg(reinterpret_cast<const uint4*>(src));
     } else {
-      __half tmp[8];
+      uint32_t w[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) tmp[j] = (k + j < L) ? src[j] : __float2half(0.f);
-      c.v[h] = *reinterpret_cast<const uint4*>(tmp);
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t lo16 = (k + 2 * j < L) ? uint32_t(__half_as_ushort(src[2 * j])) : 0u;
+        const uint32_t hi16 = (k + 2 * j + 1 < L) ? uint32_t(__half_as_ushort(src[2 * j + 1])) : 0u;
+        w[j] = lo16 | (hi16 << 16);
+      }
+      c.v[h] = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
   return c;
@@ -174,7 +189,8 @@ __device__ __forceinline__ int next_tile(uint32_t mask, int kt) {
   return rest ? __ffs(int(rest)) - 1 : -1;
 }
 
-// 18 warps per CTA: an SM sub-partition holds up to 5 of them (<= 96 registers/thread).
+// 4 * kParts + 2 warps per CTA; with kParts = 2 (10 warps) an SM sub-partition holds at
+// most 3 of them, leaving 168 registers per thread.
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_pos,
                         const __half* __restrict__ key_mask, const int32_t* __restrict__ rel_table,
@@ -324,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kt = next_tile(tmask, -1); kt >= 0; kt = next_tile(tmask, kt), ++np) {
           const int buf = np & 1;
           const uint32_t par = uint32_t(np & 1);
+          const bool first_pair = first;
           ok = ptx::mbar_wait(&bars[kBarKV0 + buf], uint32_t((np >> 1) & 1), err);
           if (ok && first) ok = ptx::mbar_wait(&bars[kBarQ], uint32_t(item_idx & 1), err);
           first = false;
@@ -347,14 +364,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::umma_f16_ss(tbase + kColCP, ptx::desc_kmajor_sw128(aK + k * 32),
                              ptx::desc_kmajor_sw128(aPQ + k * 32), id_cp, k > 0);
           ptx::umma_commit(&bars[kBarP]);
+          // probabilities written and O rescaled to this pair's running max
           if (!(ok = ptx::mbar_wait(&bars[kBarProbs], par, err))) break;
-          // O of the previous pair has been read out of TMEM
-          if (np > 0 && !(ok = ptx::mbar_wait(&bars[kBarODone], par ^ 1u, err))) break;
+          // the previous item's O has been read out of TMEM before this item overwrites it
+          if (first_pair && item_idx > 0 &&
+              !(ok = ptx::mbar_wait(&bars[kBarODone], uint32_t((item_idx - 1) & 1), err)))
+            break;
           ptx::tc_fence_after();
 #pragma unroll
           for (int s = 0; s < 8; ++s)
             ptx::umma_f16_ss(tbase + kColO, ptx::desc_kmajor_sw128(aProb + (s >> 2) * 16384 + (s & 3) * 32),
-                             ptx::desc_mnmajor_sw128(aV + s * 2048), id_pv, s > 0);
+                             ptx::desc_mnmajor_sw128(aV + s * 2048), id_pv, (s > 0 || !first_pair) ? 1u : 0u);
           ptx::umma_commit(&bars[kBarO]);
           ptx::umma_commit(&bars[kBarKVFree0 + buf]);
         }
@@ -389,10 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       const uint32_t tmask = s_flags[item_idx & 1];
-      float o[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) o[i] = 0.f;
       float m_run = -INFINITY, l_part = 0.f;
+      bool first_pair = true;
       for (int kt = next_tile(tmask, -1); kt >= 0; kt = next_tile(tmask, kt), ++np) {
         const int k0 = kt * kTile;
         const int lo = window_lo(q0, k0);
@@ -407,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        drain_rows_f16(lane_base + kColCP + part * 64, sC, t, part * 64);
+        drain_rows_f16(lane_base + kColCP + part * kColsPP, sC, t, part * kColsPP);
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&bars[kBarCDone]);
@@ -417,34 +435,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        drain_rows_f16(lane_base + kColCP + part * 64, sPst, t, part * 64);
+        drain_rows_f16(lane_base + kColCP + part * kColsPP, sPst, t, part * kColsPP);
         ptx::tc_fence_before();
         if (!rs.sync(err)) {
           ok = false;
           break;
         }
-        // ---- scores of keys [part*32, part*32 + 32) with the gathered relative bias
+        // ---- scores of keys [part*kKeysPP, +kKeysPP) with the gathered relative bias
         const int16_t* tab_q = s_tab + (q - k0 + 511);  // tab_q[-kk] = i(q - (k0 + kk))
-        float sc[32];
+        // final scores go back into this lane's S columns (TMEM), not registers
         float part_max = -INFINITY;
-        {
+#pragma unroll
+        for (int c = 0; c < kKeysPP / 32; ++c) {
           uint32_t sraw[32];
-          ptx::tmem_ld_32x32b_x32(lane_base + kColS + part * 32, sraw);
+          ptx::tmem_ld_32x32b_x32(lane_base + kColS + part * kKeysPP + c * 32, sraw);
           ptx::tmem_wait_ld();
 #pragma unroll
           for (int u = 0; u < 32; ++u) {
-            const int kk = part * 32 + u;
+            const int kk = part * kKeysPP + c * 32 + u;
             const uint32_t w2 = uint32_t(int(tab_q[-kk]) - lo) << 1;  // 2 * window column
             const __half cv = *reinterpret_cast<const __half*>(sC + c_row + (w2 ^ c_xor));
             const __half pv =
                 *reinterpret_cast<const __half*>(sPst + uint32_t(kk) * 512u + (w2 ^ (uint32_t(kk & 7) << 4)));
             const float rb = __half2float(__float2half_rn(__half2float(__hadd(cv, pv)) * kInvScale16));
             const float add = s_add[kk];
-            const float s = fmaf(__uint_as_float(sraw[u]), kInvSqrt192f, add == 0.f ? rb : add);
-            sc[u] = s;
-            part_max = fmaxf(part_max, s);
+            const float sv = fmaf(__uint_as_float(sraw[u]), kInvSqrt192f, add == 0.f ? rb : add);
+            sraw[u] = __float_as_uint(sv);
+            part_max = fmaxf(part_max, sv);
           }
+          ptx::tmem_st_32x32b_x32(lane_base + kColS + part * kKeysPP + c * 32, sraw);
         }
+        ptx::tmem_wait_st();
         s_red[part * 128 + t] = part_max;
         // every row is past its C / P reads (probabilities overwrite the C rows, the next
         // pair's windows the P rows) and all parts' maxima are visible
@@ -452,52 +473,81 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        const float m_tile =
-            fmaxf(fmaxf(s_red[t], s_red[128 + t]), fmaxf(s_red[256 + t], s_red[384 + t]));
+        float m_tile = s_red[t];
+#pragma unroll
+        for (int pp = 1; pp < kParts; ++pp) m_tile = fmaxf(m_tile, s_red[pp * 128 + t]);
         const float m_new = fmaxf(m_run, m_tile);
         const float alpha = __expf(m_run - m_new);
         float psum = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t pk[4];
+        for (int c = 0; c < kKeysPP / 32; ++c) {
+          uint32_t sv[32];
+          ptx::tmem_ld_32x32b_x32(lane_base + kColS + part * kKeysPP + c * 32, sv);
+          ptx::tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = j * 8 + 2 * e;
-            const __half2 p2 = __floats2half2_rn(__expf(sc[i] - m_new), __expf(sc[i + 1] - m_new));
-            const float2 pf = __half22float2(p2);
-            psum += pf.x + pf.y;
-            pk[e] = *reinterpret_cast<const uint32_t*>(&p2);
+          for (int j = 0; j < 4; ++j) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = j * 8 + 2 * e;
+              const __half2 p2 = __floats2half2_rn(__expf(__uint_as_float(sv[i]) - m_new),
+                                                   __expf(__uint_as_float(sv[i + 1]) - m_new));
+              const float2 pf = __half22float2(p2);
+              psum += pf.x + pf.y;
+              pk[e] = *reinterpret_cast<const uint32_t*>(&p2);
+            }
+            // K-major SW128 operand: atom kb / 64 holds keys 64*(kb/64)..+63 of row t
+            const int kb = part * kKeysPP + c * 32 + j * 8;
+            const uint32_t ch = uint32_t((kb & 63) >> 3);
+            const uint32_t off = uint32_t(kb >> 6) * 16384u + uint32_t(t >> 3) * 1024u + uint32_t(t & 7) * 128u +
+                                 ((ch ^ uint32_t(t & 7)) << 4);
+            *reinterpret_cast<uint4*>(sC + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
-          // K-major SW128 operand: atom part/2 holds keys 64*(part/2)..+63 of row t
-          const uint32_t c = uint32_t((part & 1) * 4 + j);
-          const uint32_t off = uint32_t(part >> 1) * 16384u + uint32_t(t >> 3) * 1024u + uint32_t(t & 7) * 128u +
-                               ((c ^ uint32_t(t & 7)) << 4);
-          *reinterpret_cast<uint4*>(sC + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
         ptx::fence_proxy_async_smem();
+        // ---- O accumulates in TMEM across the item's pairs: rescale it to the new running
+        // max before this pair's PV (skipped when no row of the warp changed its max)
+        if (!first_pair) {
+          if (!ptx::mbar_wait_sleep(&bars[kBarO], par ^ 1u, err)) {  // PV of the previous pair done
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          if (!__all_sync(0xffffffffu, alpha == 1.0f)) {
+            uint32_t r[kOPP];
+            tmem_ld_cols(lane_base + kColO + part * kOPP, r);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int u = 0; u < kOPP; ++u) r[u] = __float_as_uint(__uint_as_float(r[u]) * alpha);
+            tmem_st_cols(lane_base + kColO + part * kOPP, r);
+            ptx::tmem_wait_st();
+          }
+        }
+        ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&bars[kBarProbs]);
         l_part = l_part * alpha + psum;
         m_run = m_new;
-        // ---- accumulate this part's 16 columns of O_j
-        if (!ptx::mbar_wait_sleep(&bars[kBarO], par, err)) {
-          ok = false;
-          break;
-        }
-        ptx::tc_fence_after();
-        {
-          uint32_t r[16];
-          ptx::tmem_ld_32x32b_x16(lane_base + kColO + part * 16, r);
-          ptx::tmem_wait_ld();
-#pragma unroll
-          for (int u = 0; u < 16; ++u) o[u] = o[u] * alpha + __uint_as_float(r[u]);
-        }
-        ptx::tc_fence_before();
-        ptx::fence_proxy_async_smem();  // generic P-row / C-row writes precede later TMA / MMA use
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&bars[kBarODone]);
+        first_pair = false;
       }
       if (!ok) break;
+      // ---- read this part's O columns after the item's last PV
+      if (!ptx::mbar_wait_sleep(&bars[kBarO], uint32_t((np - 1) & 1), err)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      float o[kOPP];
+      {
+        uint32_t r[kOPP];
+        tmem_ld_cols(lane_base + kColO + part * kOPP, r);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < kOPP; ++u) o[u] = __uint_as_float(r[u]);
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars[kBarODone]);
       // combine the parts' softmax denominators and store this part's 16 columns
       s_red_l[part * 128 + t] = l_part;
       if (!rs.sync(err)) {
@@ -505,10 +555,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       if (q < L) {
-        const float inv = 1.0f / ((s_red_l[t] + s_red_l[128 + t]) + (s_red_l[256 + t] + s_red_l[384 + t]));
-        __half* dst = ctx + (row0 + q) * (long long)E + it.h * 64 + part * 16;
+        float lsum = s_red_l[t];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int pp = 1; pp < kParts; ++pp) lsum += s_red_l[pp * 128 + t];
+        const float inv = 1.0f / lsum;
+        __half* dst = ctx + (row0 + q) * (long long)E + it.h * 64 + part * kOPP;
+#pragma unroll
+        for (int c = 0; c < kOPP / 8; ++c) {
           uint4 v;
           v.x = ptx::pack_half2(o[c * 8 + 0] * inv, o[c * 8 + 1] * inv);
           v.y = ptx::pack_half2(o[c * 8 + 2] * inv, o[c * 8 + 3] * inv);
