@@ -74,6 +74,7 @@ SIGNATURES = [
     ("gdc_residual_layer_norm", C.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _f32, _vp]),
     ("gdc_disentangled_attention", C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     ("gdc_disentangled_attention_scalar", C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    ("gdc_disentangled_attention_noalloc", C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     ("gdc_linear", C.c_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i64, _i32, _vp]),
     ("gdc_kernels_check_errors", C.c_int, []),
     ("gdc_last_error", C.c_char_p, []),

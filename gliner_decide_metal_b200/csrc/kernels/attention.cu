@@ -5,6 +5,9 @@
 // cannot reach; the forward never calls it.
 #include <cuda.h>
 
+#include <mutex>
+
+#include "../model.h"
 #include "attention_simt.cuh"
 #include "attention_tc.cuh"
 #include "kernels.h"
@@ -53,4 +56,78 @@ gdc_status launch_attention(const __half* qkv, const __half* pos_qk, const __hal
   return check_launch("attention_tc_kernel");
 }
 
+namespace {
+
+// Allocation-free attention: the kernel's scratch (the relative index table and the
+// device-side status word that gdc_disentangled_attention keeps in cudaMalloc'd
+// memory) lives in this file-scope array instead. It is 4352 bytes and every device
+// that loads the library holds it until the process exits.
+//   [0, 1023)     relative index table, index q - k + 511 (covers seq_len <= 512)
+//   [1024]        status word; bounded-wait timeouts set bits in it
+constexpr int kStaticTableEntries = 1023;
+constexpr int kStaticStatusOffset = 1024;
+constexpr int kStaticWords = 1088;
+static __device__ __align__(256) int32_t g_attention_scratch[kStaticWords];
+
+std::mutex g_static_mu;
+int32_t* g_static_scratch[64] = {};  // device address of g_attention_scratch, per device
+
+// Once per device, with that device current: resolve the array's device address and
+// write the relative index table into it (a synchronous copy from host memory).
+gdc_status static_scratch(int32_t** out) {
+  int dev = 0;
+  GDC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(GDC_ERR_CUDA, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_scratch[dev]) {
+    int32_t* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_attention_scratch);
+    if (e != cudaSuccess)
+      return set_error(GDC_ERR_CUDA, "cudaGetSymbolAddress(attention scratch): %s", cudaGetErrorString(e));
+    int32_t table[kStaticTableEntries];
+    build_relative_table(256, 512, table);
+    GDC_CUDA_TRY(cudaMemcpy(ptr, table, sizeof(table), cudaMemcpyHostToDevice));
+    GDC_CUDA_TRY(cudaMemset(ptr + kStaticStatusOffset, 0, sizeof(int32_t)));
+    g_static_scratch[dev] = ptr;
+  }
+  *out = g_static_scratch[dev];
+  return GDC_OK;
+}
+
+}  // namespace
+
 }  // namespace gdc
+
+extern "C" gdc_status gdc_disentangled_attention_noalloc(const uint16_t* qkv, const uint16_t* pos_qk,
+                                                         const uint16_t* key_mask, uint16_t* ctx, int32_t batch,
+                                                         int32_t seq_len, int32_t heads, void* stream) {
+  using namespace gdc;
+  clear_error();
+  if (!qkv || !pos_qk || !key_mask || !ctx)
+    return set_error(GDC_ERR_NULL_POINTER, "gdc_disentangled_attention_noalloc: null argument");
+  if (heads != 16) return set_error(GDC_ERR_UNSUPPORTED, "gdc_disentangled_attention_noalloc: heads must be 16");
+  if (batch <= 0 || seq_len <= 0)
+    return set_error(GDC_ERR_INVALID_INPUT, "gdc_disentangled_attention_noalloc: batch and seq_len must be > 0");
+  if (seq_len > 512)
+    return set_error(GDC_ERR_UNSUPPORTED,
+                     "gdc_disentangled_attention_noalloc: seq_len %d exceeds the static scratch limit of 512 "
+                     "(its relative index table has %d entries)",
+                     seq_len, kStaticTableEntries);
+  int32_t* scratch = nullptr;
+  GDC_TRY(static_scratch(&scratch));
+  int32_t* status = scratch + kStaticStatusOffset;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  GDC_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int32_t), s));
+  GDC_TRY(launch_attention(reinterpret_cast<const __half*>(qkv), reinterpret_cast<const __half*>(pos_qk),
+                           reinterpret_cast<const __half*>(key_mask), scratch, reinterpret_cast<__half*>(ctx), batch,
+                           seq_len, heads, s, status));
+  int32_t h = 0;
+  GDC_CUDA_TRY(cudaMemcpyAsync(&h, status, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  GDC_CUDA_TRY(cudaStreamSynchronize(s));
+  if (h != 0) {
+    if (h & kErrTimeout)
+      return set_error(GDC_ERR_TIMEOUT, "gdc_disentangled_attention_noalloc: a device-side wait exceeded its limit");
+    return set_error(GDC_ERR_CUDA, "gdc_disentangled_attention_noalloc: device status word 0x%x", h);
+  }
+  return GDC_OK;
+}

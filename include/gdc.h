@@ -267,6 +267,27 @@ gdc_status gdc_disentangled_attention_scalar(const uint16_t* qkv, const uint16_t
                                              const uint16_t* key_mask, uint16_t* ctx, int32_t batch,
                                              int32_t seq_len, int32_t heads, void* stream);
 
+/* Allocation-free variant of gdc_disentangled_attention; it has no counterpart in the
+ * reference. Same arguments, layout and results. It is for callers that cannot let a
+ * library call cudaMalloc: hosts that reserve all device memory for their own pool up
+ * front, or that must not take the implicit device synchronisation and address-space
+ * change of an allocation in the middle of their run. The kernel's scratch (the relative
+ * index table and a status word, 4352 bytes) is a file-scope __device__ array that every
+ * device loading this library holds until the process exits; nothing here calls
+ * cudaMalloc, cudaFree or an allocating library routine.
+ *  - Limit: seq_len <= 512 (the table in the static array covers |q - k| <= 511);
+ *    larger values return GDC_ERR_UNSUPPORTED. heads must be 16.
+ *  - The first call on a device sets the array up (resolves its device address and
+ *    copies the table in, synchronously); make that first call before any stream capture.
+ *  - Each call clears the status word on `stream`, launches, reads the status word back
+ *    and synchronises `stream`, so it returns once the kernel has finished; a bounded-wait
+ *    timeout is returned as GDC_ERR_TIMEOUT.
+ *  - All calls on a device share the array and it keeps the last call's contents. Calls
+ *    that overlap on the GPU (different streams or host threads) race on the status word. */
+gdc_status gdc_disentangled_attention_noalloc(const uint16_t* qkv, const uint16_t* pos_qk,
+                                              const uint16_t* key_mask, uint16_t* ctx, int32_t batch,
+                                              int32_t seq_len, int32_t heads, void* stream);
+
 /* addMM(bias, x, W^T) (DeBERTa.swift:69-71, 89-91) on tcgen05 tensor cores:
  * out[M,N] = act(a[M,K] . w[N,K]^T + bias[N]) in fp16 with fp32 accumulation;
  * act: 0 = none, 1 = exact-erf GELU, 2 = ReLU. N must be a multiple of 256 and K a
