@@ -48,6 +48,10 @@ N_RESIDENT_BATCHES = 8
 # Algorithmic FLOPs of the four encoder projections per token (QKV 3072, out 1024,
 # FFN up 4096, FFN down 4096 outputs; K = 1024 / 1024 / 1024 / 4096), 24 layers.
 GEMM_FLOPS_PER_TOKEN = 2 * (3 * HIDDEN * HIDDEN + HIDDEN * HIDDEN + 2 * HIDDEN * INTER) * LAYERS
+# algorithmic bytes of one layer's four projections: A read + output written per token,
+# and the weights + biases once
+GEMM_BYTES_PER_TOKEN = 2 * ((HIDDEN + 3 * HIDDEN) + (HIDDEN + HIDDEN) + (HIDDEN + INTER) + (INTER + HIDDEN))
+GEMM_WEIGHT_BYTES = 2 * (3 * HIDDEN * HIDDEN + HIDDEN * HIDDEN + 2 * HIDDEN * INTER + 5 * HIDDEN + INTER)
 ATTN_FLOPS_PER_SEQ = LAYERS * 16 * 4 * 2 * SEQ * SEQ * 64  # QK, c2p, p2c, PV as gathered dots
 
 
@@ -337,13 +341,18 @@ def main():
             traffic = json.loads(tpath.read_text()).get("bytes_per_launch")
         except Exception:
             traffic = None
-    roofline = {"kernel": "gemm_tn_kernel (QKV / out / FFN-up / FFN-down projections)", "bound": "tensor",
+    roofline = {"kernel": "gemm_pair_kernel (cta_group::2 tcgen05; QKV / out / FFN-up / FFN-down projections)",
+                "bound": "tensor",
                 "measured_in": f"second pass of the same {args.steps} steps with CUDA events between kernel "
                                f"groups on the model stream ({ms_prof / args.steps:.3f} ms/step instrumented)",
                 "achieved": achieved_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": (achieved_tflops / peaks["bf16_tflops_sustained"]) if achieved_tflops else None,
                 "peak_source": f"{peaks['source']} bf16_tflops_sustained (kernel timed inside a long step)",
-                "traffic": traffic, "launches": gemm_launches,
+                "traffic": traffic,
+                "traffic_source": "profiles/gemm_traffic.json: ncu dram__bytes_read.sum + dram__bytes_write.sum per "
+                                  "launch, layer-0 projections of this workload averaged",
+                "algorithmic_bytes_per_launch_avg": GEMM_BYTES_PER_TOKEN * BATCH * SEQ / 4 + GEMM_WEIGHT_BYTES / 4,
+                "launches": gemm_launches,
                 "flops_per_launch_avg": gemm_flops / max(1, gemm_launches),
                 "kernel_ms_per_step": kernel_ms_per_step, "kernel_share": kernel_share}
     attn_ns = prof.get("attention", (0, 0))[0]
