@@ -315,6 +315,21 @@ gdc_status make_tmap_2d(void* map_out, const __half* base, uint64_t rows, uint64
   return GDC_OK;
 }
 
+gdc_status make_tmap_2d_out32(void* map_out, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld) {
+  CUtensorMap* map = static_cast<CUtensorMap*>(map_out);
+  auto fn = get_encode_fn();
+  if (!fn) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * sizeof(__half)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", int(r));
+  return GDC_OK;
+}
+
 int device_sm_count(int device) {
   static int counts[64] = {};
   if (device < 0 || device >= 64) return 148;

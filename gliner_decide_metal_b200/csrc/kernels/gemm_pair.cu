@@ -32,7 +32,8 @@ struct PairShape {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (200 * 1024) / kStageBytes;
   static constexpr int kTmemCols = (2 * BN <= 256) ? 256 : 512;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kOutBytes = kEpiWarps * 2048;    // per epilogue warp: a 32 x 32 fp16 store box
+  static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 + 256;
 };
 
 // erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26
@@ -50,14 +51,15 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + e
 template <int BN, int ACT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                     const __half* __restrict__ bias, __half* __restrict__ out, int M, int N, int K, long long ldo,
+                     const __grid_constant__ CUtensorMap tm_out, const __half* __restrict__ bias, int M, int N, int K,
                      int* err) {
   using S = PairShape<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
   uint8_t* s_b = smem + S::kStages * S::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_b + S::kStages * S::kBBytes);
+  uint8_t* s_out = s_b + S::kStages * S::kBBytes;  // epilogue store boxes (1024-aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_out + S::kOutBytes);
   uint64_t* empty = full + S::kStages;
   uint64_t* tfull = empty + S::kStages;
   uint64_t* tempty = tfull + 2;
@@ -187,9 +189,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     // Epilogue warps 2..(1 + kEpiWarps): TMEM lane quarter warp % 4, column half (warp-2)/4.
+    // Each 32-row x 32-column chunk goes through this warp's 2 KB box in shared memory
+    // (64-byte swizzle) and out with one TMA tensor store: full-line global writes instead
+    // of 16-byte stores to 32 different rows.
     const int quarter = warp & 3;
     const int col_half = (warp - 2) >> 2;
     constexpr int kHalfCols = BN / 2;
+    uint8_t* box = s_out + (warp - 2) * 2048;
+    uint8_t* box_row = box + lane * 64;
+    const uint32_t box_swz = uint32_t((lane >> 1) & 3);
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
       const int acc = local & 1;
@@ -198,7 +206,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       ptx::tc_fence_after();
       const int mb = tile % num_m;
       const int nb = tile / num_m;
-      const int row = mb * 256 + int(rank) * 128 + quarter * 32 + lane;
+      const int row0 = mb * 256 + int(rank) * 128 + quarter * 32;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < kHalfCols; c += 32) {
@@ -228,17 +236,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             packed[q * 4 + j] = ptx::pack_half2(v0, v1);
           }
         }
-        if (row < M) {
-          uint4* dst = reinterpret_cast<uint4*>(out + (long long)row * ldo + n0);
+        // the previous chunk's store has finished reading the box
+        if (lane == 0) ptx::bulk_wait_group_read0();
+        __syncwarp();
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(packed[q * 4], packed[q * 4 + 1], packed[q * 4 + 2], packed[q * 4 + 3]);
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(box_row + ((uint32_t(q) ^ box_swz) << 4)) =
+              make_uint4(packed[q * 4], packed[q * 4 + 1], packed[q * 4 + 2], packed[q * 4 + 3]);
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::tma_store_2d(&tm_out, n0, row0, box);
+          ptx::bulk_commit_group();
         }
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&tempty[acc]), 0));
     }
+    if (lane == 0) ptx::bulk_wait_group0();  // this warp's stores are complete before the CTA exits
   }
 
   ptx::tc_fence_before();
@@ -251,8 +267,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, int ACT>
-gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, const __half* bias, __half* out,
-                               long long ldo, int M, int N, int K, cudaStream_t stream, int* err) {
+gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const __half* bias,
+                               int M, int N, int K, cudaStream_t stream, int* err) {
   using S = PairShape<BN>;
   auto kern = gemm_pair_kernel<BN, ACT>;
   static bool configured[64] = {};
@@ -266,7 +282,7 @@ gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, con
   const int num_tiles = ((M + 255) / 256) * (N / BN);
   const int pairs_avail = device_sm_count(dev) / 2;
   const int pairs = num_tiles < pairs_avail ? num_tiles : pairs_avail;
-  kern<<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(ta, tw, bias, out, M, N, K, ldo, err);
+  kern<<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(ta, tw, to, bias, M, N, K, err);
   return check_launch("gemm_pair_kernel");
 }
 
@@ -296,15 +312,16 @@ gdc_status launch_linear_pair(const __half* a, int64_t lda, const __half* w, con
   cudaGetDevice(&dev);
   const int bn = choose_bn(M, N, device_sm_count(dev) / 2);
   if (bn == 0) return set_error(GDC_ERR_UNSUPPORTED, "linear: N=%d is not a multiple of 128", N);
-  CUtensorMap ta, tw;
+  CUtensorMap ta, tw, to;
   GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), 128));
   GDC_TRY(make_tmap_2d(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 2)));
+  GDC_TRY(make_tmap_2d_out32(&to, out, uint64_t(M), uint64_t(N), uint64_t(ldo)));
   const int m = int(M);
 #define GDC_PAIR_CASE(BNV)                                                                              \
   if (bn == BNV) {                                                                                      \
-    if (act == kActGelu) return launch_pair_variant<BNV, kActGelu>(ta, tw, bias, out, ldo, m, N, K, stream, err); \
-    if (act == kActRelu) return launch_pair_variant<BNV, kActRelu>(ta, tw, bias, out, ldo, m, N, K, stream, err); \
-    return launch_pair_variant<BNV, kActNone>(ta, tw, bias, out, ldo, m, N, K, stream, err);          \
+    if (act == kActGelu) return launch_pair_variant<BNV, kActGelu>(ta, tw, to, bias, m, N, K, stream, err); \
+    if (act == kActRelu) return launch_pair_variant<BNV, kActRelu>(ta, tw, to, bias, m, N, K, stream, err); \
+    return launch_pair_variant<BNV, kActNone>(ta, tw, to, bias, m, N, K, stream, err);          \
   }
   GDC_PAIR_CASE(256)
   GDC_PAIR_CASE(192)

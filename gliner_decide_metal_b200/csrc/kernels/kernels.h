@@ -64,4 +64,8 @@ int device_sm_count(int device);
 gdc_status make_tmap_2d(void* map, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld,
                         uint32_t box_rows);
 
+// 2-D fp16 TMA descriptor for 32 x 32 output boxes (64-byte rows, 64-byte swizzle), used by
+// the GEMM epilogue's tensor stores; rows / columns beyond the extent are not written.
+gdc_status make_tmap_2d_out32(void* map, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld);
+
 }  // namespace gdc

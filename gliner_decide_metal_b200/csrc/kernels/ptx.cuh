@@ -125,6 +125,24 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tensor_m
       : "memory");
 }
 
+// 2-D tiled bulk tensor store shared -> global (bulk-group completion). Rows and columns
+// outside the tensor map's extent are not written.
+__device__ __forceinline__ void tma_store_2d(const void* tensor_map, int32_t x, int32_t y, const void* smem_src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(reinterpret_cast<uint64_t>(tensor_map)), "r"(x), "r"(y), "r"(smem_u32(smem_src))
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until every committed bulk store of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Waits until every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tensor_map(const void* tensor_map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tensor_map)) : "memory");
 }
