@@ -67,6 +67,18 @@ struct Workspace {
   size_t h_in_bytes = 0;
   uint8_t* h_out = nullptr;
   size_t h_out_bytes = 0;
+  int generation = 0;  // bumped whenever a device buffer above is reallocated
+};
+
+// A captured forward for one input shape, replayed with cudaGraphLaunch. It reads the
+// workspace staging buffers (ids, mask, marker_idx, marker_mask) and writes
+// ws.logits / ws.logits16; valid while the workspace generation is unchanged.
+struct ForwardGraph {
+  int batch = 0, seq_len = 0, max_heads = 0, max_options = 0;
+  int generation = -1;
+  int calls = 0;                  // eager calls seen for this shape (captured on the second)
+  cudaGraphExec_t exec = nullptr;
+  uint64_t last_use = 0;
 };
 
 }  // namespace gdc
@@ -99,6 +111,10 @@ struct gdc_model {
   int* err = nullptr;            // device error word
 
   gdc::Workspace ws;
+
+  // captured forwards (small LRU keyed by input shape); GDC_GRAPHS=0 disables them
+  std::vector<gdc::ForwardGraph> graphs;
+  uint64_t graph_clock = 0;
 
   // stage profiler (events bracket kernel groups)
   bool profiling = false;

@@ -128,6 +128,38 @@ def test_profile_events_and_determinism(weights_file):
     model.close()
 
 
+def test_graph_replay_matches_eager(weights_file):
+    """The first classify of a shape runs the kernels eagerly, the second captures a CUDA
+    graph, later ones replay it: all bit-identical, also across an interleaved second
+    shape and through gdc_classify_device with caller buffers at other addresses."""
+    import torch
+    import gliner_decide_metal_b200 as g
+    model, _ = _model(weights_file, 7, 2, 1000)
+    gld = load_golden("ragged_B3_L40_2L")
+    inp = g.DecisionInput(gld["input_ids"], gld["attention_mask"], gld["marker_indices"], gld["marker_mask"])
+    other = g.DecisionInput(gld["input_ids"][:2], gld["attention_mask"][:2], gld["marker_indices"][:2],
+                            gld["marker_mask"][:2])
+    runs = []
+    for i in range(4):
+        runs.append(model.classify(inp).logits_f32)
+        if i == 1:
+            assert np.array_equal(model.classify(other).logits_f32, model.classify(other).logits_f32)
+    for r in runs[1:]:
+        assert np.array_equal(runs[0], r)
+    B, L = inp.input_ids.shape
+    _, Hm, O = inp.marker_indices.shape
+    dev = [torch.from_numpy(np.ascontiguousarray(x)).cuda() for x in (
+        inp.input_ids.astype(np.int32), inp.attention_mask.astype(np.float16),
+        inp.marker_indices.astype(np.int32), inp.marker_mask.astype(np.float32))]
+    for _ in range(3):
+        logits = torch.full((B, Hm, O), float("nan"), dtype=torch.float32, device="cuda")
+        model.classify_device(B, L, Hm, O, *(t.data_ptr() for t in dev), logits.data_ptr(),
+                              stream=model.stream)
+        torch.cuda.synchronize()
+        assert np.array_equal(logits.cpu().numpy(), runs[0])
+    model.close()
+
+
 def test_sharded_equals_single(weights_file):
     """classify_sharded over two handles (same device here) equals a single classify."""
     import gliner_decide_metal_b200 as g
