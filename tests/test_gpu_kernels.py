@@ -99,7 +99,8 @@ def test_linear_leading_dimension():
 
 
 @pytest.mark.parametrize("rows,cols,with_res", [(1, 1024, True), (37, 1024, True), (8192, 1024, True),
-                                                 (64, 256, False), (3, 4096, True)])
+                                                 (64, 256, False), (3, 4096, True), (1500, 512, True),
+                                                 (4099, 768, False), (2048, 256, True)])
 def test_residual_layer_norm(rows, cols, with_res):
     torch = _torch()
     rng = np.random.Generator(np.random.PCG64(rows + cols))
