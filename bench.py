@@ -177,21 +177,27 @@ def run_reference_arm(args, rank):
 class ClockSampler:
     """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, devices):
-        self.devices = devices
+    def __init__(self, uuids):
+        # GPUs of this job by UUID (nvidia-smi numbers GPUs physically, CUDA by visibility)
+        self.uuids = {str(u).lower().removeprefix("gpu-") for u in uuids}
         self.proc = None
+        self.window = None
         self.path = Path(tempfile.gettempdir()) / f"gdc_clocks_{os.getpid()}.csv"
 
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                                          "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+
+    def mark(self, t0: float, t1: float):
+        """Wall-clock bounds of the timed region; only samples inside it are kept."""
+        self.window = (t0, t1)
 
     def stop(self):
         if not self.proc:
@@ -201,25 +207,27 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        import datetime
+        rows = []
         for line in self.path.read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10 or parts[1].lower().removeprefix("gpu-") not in self.uuids:
                 continue
             try:
-                if int(parts[0]) not in self.devices:
-                    continue
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]), parts[6:10]))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+        if self.window is not None:
+            t0, t1 = self.window
+            inside = [r for r in rows if t0 <= r[0] <= t1 + 0.1]
+            rows = inside or [r for r in rows if r[0] >= t0][:len(self.uuids)]
+        if not rows:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = {n for r in rows for n, v in zip(names, r[3]) if v.lower() == "active"}
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": rows[-1][2],
+                "reasons": sorted(reasons), "samples": len(rows)}
 
 
 # ----------------------------------------------------------------------------- native arm
@@ -285,21 +293,27 @@ def main():
         torch.cuda.synchronize(local)
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
+        wall[0] = time.time()
         ev0.record(stream)
         for i in range(args.steps):
             step(i)
         ev1.record(stream)
         torch.cuda.synchronize(local)
+        wall[1] = time.time()
         barrier()
         if profiled:
             model.profile_enable(False)
         return ev0.elapsed_time(ev1)
 
+    wall = [0.0, 0.0]
+
     # ---- timed region (device), clocks sampled during it
-    clocks = ClockSampler(list(range(torch.cuda.device_count())) if world > 1 else [local])
+    devs = list(range(torch.cuda.device_count())) if world > 1 else [local]
+    clocks = ClockSampler([torch.cuda.get_device_properties(d).uuid for d in devs])
     clocks.start()
     time.sleep(0.4)  # let the sampler start before the load
     ms = timed_region(False)
+    clocks.mark(wall[0], wall[1])
     clk = clocks.stop()
     model.check_errors()
     ms_max = max_over_ranks(ms)
