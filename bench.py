@@ -221,6 +221,7 @@ class ClockSampler:
         if self.window is not None:
             t0, t1 = self.window
             inside = [r for r in rows if t0 <= r[0] <= t1 + 0.1]
+            # a region shorter than the sampling period: the first samples after its start
             rows = inside or [r for r in rows if r[0] >= t0][:len(self.uuids)]
         if not rows:
             return None
@@ -314,6 +315,7 @@ def main():
     time.sleep(0.4)  # let the sampler start before the load
     ms = timed_region(False)
     clocks.mark(wall[0], wall[1])
+    time.sleep(0.3)  # let the sampler flush the samples of a short timed region
     clk = clocks.stop()
     model.check_errors()
     ms_max = max_over_ranks(ms)
