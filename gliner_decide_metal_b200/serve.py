@@ -1,0 +1,158 @@
+"""Batch serving loop of the reference's raw CLI (RawCLI.swift:104-171) over pre-tokenised
+examples.
+
+The reference reads JSONL lines ``{id, text, tasks}``, tokenises each with
+``NativeDecisionTokenizer.makeInput`` (NativeTokenizer.swift:76-264), groups the inputs by
+``(L, maxHeads, maxOptions)``, classifies each group in chunks of ``batch_size`` rows,
+decodes every row's tasks (RawCLI.swift:182-223) and writes a JSON array of results in
+input order, each with the inference time of its batch divided by the batch size.
+
+Tokenisation needs the model's ``tokenizer.json``, which this backend does not ship, so the
+loop here starts one step later: each example carries the token ids the tokenizer would
+produce (schema + text, before padding) and the positions of its ``[L]`` label markers per
+task. Bucket choice, padding and marker layout are the reference's (``gdc_layout_row``);
+grouping, chunking, decoding and the output format are RawCLI's. ``--devices`` splits each
+chunk's rows across GPUs (``gdc_classify_sharded``).
+
+JSONL input line::
+
+    {"id": "...", "token_ids": [...],
+     "tasks": [{"name": "...", "labels": [...], "multi_label": false, "marker_positions": [...]}]}
+
+Output (``--output`` or stdout): the reference's JSON array
+``[{"id", "predictions": [{"task", "labels", "probabilities"}], "preprocessingMilliseconds",
+"inferenceMilliseconds"}]``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+import time
+from dataclasses import dataclass
+from typing import Dict, List, Sequence, Tuple
+
+import numpy as np
+
+from . import (DEFAULT_BUCKETS, DecisionInput, DecisionTask, DeBERTaV2Configuration, GLiNERDecideClassifier,
+               Prediction, classify_sharded, decode, make_input_from_tokens)
+
+
+@dataclass
+class TokenizedExample:
+    """One JSONL line after tokenisation: full token ids (schema + text, unpadded) and, per
+    task, the positions of its label markers."""
+    id: str
+    token_ids: List[int]
+    tasks: List[DecisionTask]
+    marker_positions: List[List[int]]
+
+
+@dataclass
+class RawResult:
+    id: str
+    predictions: List[Prediction]
+    preprocessing_ms: float
+    inference_ms: float
+
+    def to_json(self) -> dict:
+        return {"id": self.id,
+                "predictions": [{"task": p.task, "labels": list(p.labels), "probabilities": list(p.probabilities)}
+                                for p in self.predictions],
+                "preprocessingMilliseconds": self.preprocessing_ms,
+                "inferenceMilliseconds": self.inference_ms}
+
+
+def parse_example(obj: dict) -> TokenizedExample:
+    tasks, markers = [], []
+    for t in obj["tasks"]:
+        tasks.append(DecisionTask(str(t["name"]), tuple(t["labels"]), bool(t.get("multi_label", False))))
+        markers.append([int(p) for p in t["marker_positions"]])
+    return TokenizedExample(str(obj["id"]), [int(x) for x in obj["token_ids"]], tasks, markers)
+
+
+def load_jsonl(path) -> List[TokenizedExample]:
+    with open(path, "r", encoding="utf-8") as f:
+        return [parse_example(json.loads(line)) for line in f if line.strip()]
+
+
+@dataclass
+class _Pending:
+    index: int
+    example: TokenizedExample
+    input: DecisionInput
+    preprocessing_ms: float
+
+
+def _classify(models, inp: DecisionInput) -> Tuple[np.ndarray, float]:
+    """fp32 view of the fp16 logits (as RawCLI's ``asType(.float32)``) and the batch's
+    inference milliseconds."""
+    if hasattr(models, "classify"):  # one model
+        r = models.classify(inp)
+        return r.logits_f32, r.wall_milliseconds
+    if len(models) == 1:
+        return _classify(models[0], inp)
+    t0 = time.perf_counter()
+    _, logits, _ = classify_sharded(models, inp)
+    return logits, (time.perf_counter() - t0) * 1e3
+
+
+def run_examples(models, examples: Sequence[TokenizedExample], buckets=DEFAULT_BUCKETS,
+                 batch_size: int = 32) -> List[RawResult]:
+    """RawCLI.runJSONL (RawCLI.swift:104-171) from the tokenised rows on: layout each row,
+    group by (L, maxHeads, maxOptions), classify in chunks of ``batch_size``, decode."""
+    if batch_size <= 0:
+        raise ValueError("batch_size must be positive")
+    pending: List[_Pending] = []
+    for i, ex in enumerate(examples):
+        t0 = time.perf_counter()
+        inp = make_input_from_tokens(ex.token_ids, ex.marker_positions, buckets)
+        pending.append(_Pending(i, ex, inp, (time.perf_counter() - t0) * 1e3))
+    groups: Dict[Tuple[int, int, int], List[_Pending]] = {}
+    for p in pending:
+        _, L, hm, o = p.input.shape
+        groups.setdefault((L, hm, o), []).append(p)
+    results: List[RawResult] = [None] * len(pending)  # type: ignore[list-item]
+    for group in groups.values():
+        for start in range(0, len(group), batch_size):
+            batch = group[start:start + batch_size]
+            inp = DecisionInput.concatenated([p.input for p in batch])
+            logits, ms = _classify(models, inp)
+            for row, p in enumerate(batch):
+                results[p.index] = RawResult(p.example.id, decode(logits, p.example.tasks, row), p.preprocessing_ms,
+                                             ms / len(batch))
+    return results
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(prog="python -m gliner_decide_metal_b200.serve", description=__doc__.split("\n")[0])
+    ap.add_argument("--jsonl", required=True, help="pre-tokenised examples, one JSON object per line")
+    ap.add_argument("--weights", required=True, help="fp16 safetensors weights")
+    ap.add_argument("--buckets", default=",".join(str(b) for b in DEFAULT_BUCKETS))
+    ap.add_argument("--batch-size", type=int, default=32)
+    ap.add_argument("--devices", default="0", help="comma-separated CUDA devices; rows of a chunk are split")
+    ap.add_argument("--layers", type=int, default=24, help="encoder layers in the weights file")
+    ap.add_argument("--vocab", type=int, default=128011)
+    ap.add_argument("--output", default=None)
+    args = ap.parse_args(argv)
+    buckets = [int(b) for b in args.buckets.split(",") if b]
+    cfg = DeBERTaV2Configuration(num_hidden_layers=args.layers, vocab_size=args.vocab)
+    models = [GLiNERDecideClassifier(args.weights, configuration=cfg, device=int(d)) for d in args.devices.split(",")]
+    try:
+        examples = load_jsonl(args.jsonl)
+        print(f"loaded {len(examples)} examples", file=sys.stderr)
+        results = run_examples(models, examples, buckets, args.batch_size)
+    finally:
+        for m in models:
+            m.close()
+    data = json.dumps([r.to_json() for r in results])
+    if args.output:
+        with open(args.output, "w", encoding="utf-8") as f:
+            f.write(data)
+    else:
+        print(data)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

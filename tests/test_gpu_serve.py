@@ -1,0 +1,75 @@
+"""GPU end-to-end tests beyond the bench configuration: BASELINE config 3 (mixed buckets,
+1-3 tasks of 2-12 labels, 30% multi-label) through the serving loop against the oracle, and
+config 4 (256 rows at L=512, 24 layers) through size-independent properties."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import reference_forward as rf
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_ATOL = 2e-2
+PROB_ATOL = 1e-3
+
+
+def test_config3_serving_loop_matches_oracle(weights_file):
+    import gliner_decide_metal_b200 as g
+    from gliner_decide_metal_b200 import serve, synthetic
+    layers, vocab = 2, 128011
+    path, w = weights_file(11, layers, vocab)
+    model = g.GLiNERDecideClassifier(path, configuration=g.DeBERTaV2Configuration(num_hidden_layers=layers,
+                                                                                  vocab_size=vocab))
+    ex = []
+    for i, (ids, markers, n_labels, ml) in enumerate(synthetic.mixed_rows(24, seed=21)):
+        tasks = [g.DecisionTask(f"t{h}", tuple(f"l{j}" for j in range(n)), m) for h, (n, m) in
+                 enumerate(zip(n_labels, ml))]
+        ex.append(serve.TokenizedExample(f"r{i}", [int(x) for x in ids], tasks, [list(p) for p in markers]))
+    res = serve.run_examples(model, ex, batch_size=8)
+    W = rf.OracleWeights(w, rf.OracleConfig(num_hidden_layers=layers, vocab_size=vocab))
+    buckets = set()
+    for r, e in zip(res, ex):
+        inp = g.make_input_from_tokens(e.token_ids, e.marker_positions)
+        buckets.add(inp.shape[1])
+        ref = rf.forward(W, inp.input_ids, inp.attention_mask, inp.marker_indices, inp.marker_mask)[0]
+        dec = rf.decode(ref, [len(t.labels) for t in e.tasks], [t.multi_label for t in e.tasks])
+        for p, t, (pr, sel) in zip(r.predictions, e.tasks, dec):
+            n = len(t.labels)
+            np.testing.assert_allclose(p.probabilities, pr[:n], atol=PROB_ATOL, rtol=0)
+            want = [t.labels[j] for j in sel]
+            if t.multi_label:
+                tie = np.abs(np.asarray(pr[:n]) - 0.5).min() < 2e-3
+            else:
+                srt = np.sort(pr[:n])[::-1]
+                tie = n > 1 and srt[0] - srt[1] < 2e-3
+            if not tie:
+                assert p.labels == want, (e.id, t.name)
+    assert len(buckets) >= 3  # the rows spread over several buckets
+    model.close()
+
+
+def test_config4_full_size_properties(weights_file):
+    """BASELINE config 4 (256 rows, L=512, text U[200,500], 24 layers): permuting rows
+    permutes the logits bit-exactly, a row alone equals its row in the batch, and one row
+    matches the fp16 oracle."""
+    import gliner_decide_metal_b200 as g
+    from gliner_decide_metal_b200 import synthetic
+    c4 = synthetic.config4()
+    path, w = weights_file(0, 24, 128011)
+    model = g.GLiNERDecideClassifier(path)
+    inp = g.DecisionInput(c4.input_ids, c4.attention_mask, c4.marker_indices, c4.marker_mask)
+    full = model.classify(inp).logits_f32
+    assert np.isfinite(full).all()
+    perm = np.random.Generator(np.random.PCG64(1)).permutation(len(c4.input_ids))
+    pinp = g.DecisionInput(c4.input_ids[perm], c4.attention_mask[perm], c4.marker_indices[perm],
+                           c4.marker_mask[perm])
+    assert np.array_equal(model.classify(pinp).logits_f32, full[perm])
+    one = model.classify(g.DecisionInput(c4.input_ids[200:201], c4.attention_mask[200:201],
+                                         c4.marker_indices[200:201], c4.marker_mask[200:201])).logits_f32
+    assert np.array_equal(one[0], full[200])
+    W = rf.OracleWeights(w, rf.OracleConfig())
+    ref = rf.forward(W, c4.input_ids[200:201], c4.attention_mask[200:201], c4.marker_indices[200:201],
+                     c4.marker_mask[200:201])
+    np.testing.assert_allclose(full[200:201], ref, atol=LOGIT_ATOL, rtol=0)
+    model.close()

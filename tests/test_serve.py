@@ -1,0 +1,79 @@
+"""CPU tests of the batch serving loop (gliner_decide_metal_b200/serve.py, RawCLI.swift:104-171):
+grouping by (L, maxHeads, maxOptions), chunking, input-order results, decode and the JSON
+format, with a stand-in model whose logits are a fixed function of the input."""
+from __future__ import annotations
+
+import json
+
+import numpy as np
+
+import gliner_decide_metal_b200 as g
+from gliner_decide_metal_b200 import serve, synthetic
+
+
+class _FakeModel:
+    def __init__(self):
+        self.batches = []
+
+    def classify(self, inp):
+        b, L, hm, o = inp.shape
+        self.batches.append((b, L, hm, o))
+        lg = (np.asarray(inp.marker_indices, np.float32) * 0.05 - 2.0
+              + np.asarray(inp.input_ids[:, :1], np.float32)[:, :, None] * 1e-6)
+        lg = np.where(np.asarray(inp.marker_mask) > 0, lg, -10000.0).astype(np.float16)
+        return g.InferenceResult(lg, lg.astype(np.float32), 1_000_000 * b)
+
+
+def _examples(n, seed=4):
+    out = []
+    for i, (ids, markers, n_labels, ml) in enumerate(synthetic.mixed_rows(n, seed=seed)):
+        tasks = [g.DecisionTask(f"task{h}", tuple(f"l{h}_{j}" for j in range(n)), m)
+                 for h, (n, m) in enumerate(zip(n_labels, ml))]
+        out.append(serve.TokenizedExample(f"row{i}", [int(x) for x in ids], tasks, [list(p) for p in markers]))
+    return out
+
+
+def test_groups_chunks_and_keeps_input_order():
+    ex = _examples(40)
+    model = _FakeModel()
+    res = serve.run_examples(model, ex, batch_size=4)
+    assert [r.id for r in res] == [e.id for e in ex]
+    assert all(b <= 4 for b, *_ in model.batches)
+    assert sum(b for b, *_ in model.batches) == len(ex)
+    shapes = {}
+    for e in ex:
+        inp = g.make_input_from_tokens(e.token_ids, e.marker_positions)
+        shapes.setdefault(inp.shape[1:], 0)
+        shapes[inp.shape[1:]] += 1
+    seen = {}
+    for b, L, hm, o in model.batches:
+        seen[(L, hm, o)] = seen.get((L, hm, o), 0) + b
+    assert seen == shapes  # one group per (L, maxHeads, maxOptions), every row once
+    for r, e in zip(res, ex):
+        inp = g.make_input_from_tokens(e.token_ids, e.marker_positions)
+        lg = model.classify(inp).logits_f32
+        want = g.decode(lg, e.tasks, 0)
+        assert [p.task for p in r.predictions] == [t.name for t in e.tasks]
+        for p, w in zip(r.predictions, want):
+            assert p.labels == w.labels
+            np.testing.assert_allclose(p.probabilities, w.probabilities, rtol=0, atol=0)
+        assert r.inference_ms == 1.0  # the batch's time split over its rows
+
+
+def test_jsonl_round_trip_and_output_format(tmp_path):
+    ex = _examples(6, seed=9)
+    path = tmp_path / "rows.jsonl"
+    with open(path, "w") as f:
+        for e in ex:
+            f.write(json.dumps({"id": e.id, "token_ids": e.token_ids, "tasks": [
+                {"name": t.name, "labels": list(t.labels), "multi_label": t.multi_label, "marker_positions": m}
+                for t, m in zip(e.tasks, e.marker_positions)]}) + "\n")
+    back = serve.load_jsonl(path)
+    assert [(b.id, b.token_ids, b.marker_positions) for b in back] == [(e.id, e.token_ids, e.marker_positions)
+                                                                       for e in ex]
+    assert [[(t.name, t.labels, t.multi_label) for t in b.tasks] for b in back] == \
+        [[(t.name, t.labels, t.multi_label) for t in e.tasks] for e in ex]
+    out = [r.to_json() for r in serve.run_examples(_FakeModel(), back)]
+    assert set(out[0]) == {"id", "predictions", "preprocessingMilliseconds", "inferenceMilliseconds"}
+    assert set(out[0]["predictions"][0]) == {"task", "labels", "probabilities"}
+    json.dumps(out)
