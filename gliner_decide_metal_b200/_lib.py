@@ -77,6 +77,7 @@ SIGNATURES = [
     ("gdc_disentangled_attention_noalloc", C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     ("gdc_linear", C.c_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i64, _i32, _vp]),
     ("gdc_kernels_check_errors", C.c_int, []),
+    ("gdc_selftest_wait_timeout", C.c_int, [_i32, _vp]),
     ("gdc_last_error", C.c_char_p, []),
     ("gdc_abi_version", C.c_int, []),
     ("gdc_build_info", C.c_char_p, []),

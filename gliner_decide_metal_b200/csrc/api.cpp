@@ -607,6 +607,13 @@ gdc_status gdc_linear(const uint16_t* a, const uint16_t* w, const uint16_t* bias
                        static_cast<cudaStream_t>(stream), err);
 }
 
+gdc_status gdc_selftest_wait_timeout(int32_t limit_us, void* stream) {
+  clear_error();
+  int* err = nullptr;
+  GDC_TRY(device_error_word(&err));
+  return launch_wait_timeout_probe(err, limit_us, static_cast<cudaStream_t>(stream));
+}
+
 gdc_status gdc_kernels_check_errors(void) {
   clear_error();
   int* err = nullptr;

@@ -58,6 +58,10 @@ gdc_status launch_decode(const float* logits, int batch, int max_heads, int max_
 
 int device_sm_count(int device);
 
+// Failure-detection self-test: a kernel whose bounded wait on an mbarrier that never
+// completes runs out after limit_us microseconds and sets kErrTimeout in *err.
+gdc_status launch_wait_timeout_probe(int* err, int limit_us, cudaStream_t stream);
+
 // 2-D fp16 TMA descriptor: `rows` x `cols` (cols contiguous), row pitch `ld` elements,
 // box = box_rows x 64 columns, 128-byte swizzle, out-of-bounds rows read as zero.
 // (CUtensorMap is passed as void* to keep <cuda.h> out of this header.)

@@ -299,6 +299,13 @@ gdc_status gdc_linear(const uint16_t* a, const uint16_t* w, const uint16_t* bias
  * points above (bounded-wait timeouts). Synchronises the device. */
 gdc_status gdc_kernels_check_errors(void);
 
+/* Failure-detection self-test (no counterpart in the reference): launches a kernel whose
+ * bounded wait on a barrier that nothing completes runs out after limit_us microseconds
+ * (1 .. 1e6), exactly like a stuck wait in the forward's kernels. The kernel sets the
+ * timeout bit of the current device's error word and returns, so the next
+ * gdc_kernels_check_errors() reports GDC_ERR_TIMEOUT and clears it; the device stays usable. */
+gdc_status gdc_selftest_wait_timeout(int32_t limit_us, void* stream);
+
 /* Last error message of this thread. */
 const char* gdc_last_error(void);
 

@@ -239,3 +239,28 @@ def test_attention_tensor_core_matches_scalar_kernel(B, L):
     x, y = _host(a).astype(np.float32), _host(b).astype(np.float32)
     assert np.isfinite(x).all()
     np.testing.assert_allclose(x, y, rtol=1e-2, atol=4e-3)
+
+
+def test_device_wait_timeout_is_reported_and_device_stays_usable():
+    """Failure detection without a fault: a kernel's bounded wait on a barrier that nothing
+    completes gives up after 2 ms, sets the timeout bit, returns; the host sees
+    GDC_ERR_TIMEOUT once, and the next kernel call works."""
+    torch = _torch()
+    lib = _lib()
+    assert lib.gdc_kernels_check_errors() == 0
+    _check(lib.gdc_selftest_wait_timeout(2000, None))
+    torch.cuda.synchronize()
+    assert lib.gdc_kernels_check_errors() == 9  # GDC_ERR_TIMEOUT
+    assert b"time limit" in lib.gdc_last_error()
+    assert lib.gdc_kernels_check_errors() == 0  # cleared
+    assert lib.gdc_selftest_wait_timeout(0, None) == 3  # GDC_ERR_INVALID_INPUT
+    rng = np.random.Generator(np.random.PCG64(3))
+    a = rng.standard_normal((256, 64), dtype=np.float32).astype(np.float16)
+    w = rng.standard_normal((256, 64), dtype=np.float32).astype(np.float16)
+    b = np.zeros(256, np.float16)
+    out = torch.empty((256, 256), dtype=torch.float16, device="cuda")
+    _check(lib.gdc_linear(_ptr(a), _ptr(w), _ptr(b), out.data_ptr(), 256, 256, 64, 256, 0, None))
+    torch.cuda.synchronize()
+    _check(lib.gdc_kernels_check_errors())
+    ref = a.astype(np.float64) @ w.astype(np.float64).T
+    np.testing.assert_allclose(_host(out).astype(np.float64), ref, rtol=2e-3, atol=2e-3)
