@@ -21,14 +21,20 @@
 namespace gdc {
 namespace {
 
-constexpr int kBK = 64;
+// A stage holds 128 K-columns as two 64-column (128-byte) swizzle atoms per operand, so the
+// issuing thread waits, issues 8 MMAs and commits once per 128 columns: the per-stage
+// wait / commit cost of the single issuing thread is what bounded the main loop at 64.
+constexpr int kBK = 128;
+constexpr int kAtomK = 64;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 template <int BN>
 struct PairShape {
-  static constexpr int kABytes = 128 * kBK * 2;        // this CTA's 128 rows of A
-  static constexpr int kBBytes = (BN / 2) * kBK * 2;   // this CTA's BN/2 rows of W
+  static constexpr int kAHalf = 128 * kAtomK * 2;       // one K-atom of this CTA's 128 rows of A
+  static constexpr int kBHalf = (BN / 2) * kAtomK * 2;  // one K-atom of this CTA's BN/2 rows of W
+  static constexpr int kABytes = 2 * kAHalf;
+  static constexpr int kBBytes = 2 * kBHalf;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (200 * 1024) / kStageBytes;
   static constexpr int kTmemCols = (2 * BN <= 256) ? 256 : 512;
@@ -72,7 +78,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const bool leader = rank == 0;
   const int num_m = (M + 255) / 256;
   const int num_tiles = num_m * (N / BN);
-  const int kblocks = K / kBK;
+  const int kblocks = (K + kBK - 1) / kBK;  // a last half block reads TMA zero fill
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
 
@@ -116,9 +122,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           const uint32_t leader_full = ptx::mapa_shared(ptx::smem_u32(&full[stage]), 0);
           if (leader) ptx::mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
-          ptx::tma_load_2d_pair(s_a + stage * S::kABytes, &tm_a, kb * kBK, mb * 256 + int(rank) * 128, leader_full);
-          ptx::tma_load_2d_pair(s_b + stage * S::kBBytes, &tm_w, kb * kBK, nb * BN + int(rank) * (BN / 2),
-                                leader_full);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            ptx::tma_load_2d_pair(s_a + stage * S::kABytes + h * S::kAHalf, &tm_a, kb * kBK + h * kAtomK,
+                                  mb * 256 + int(rank) * 128, leader_full);
+            ptx::tma_load_2d_pair(s_b + stage * S::kBBytes + h * S::kBHalf, &tm_w, kb * kBK + h * kAtomK,
+                                  nb * BN + int(rank) * (BN / 2), leader_full);
+          }
           ++issued;
           if (++stage == S::kStages) {
             stage = 0;
@@ -166,21 +176,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = ptx::smem_u32(s_a + stage * S::kABytes);
           const uint32_t b_addr = ptx::smem_u32(s_b + stage * S::kBBytes);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)
-            ptx::umma_f16_ss_pair(d_tmem, ptx::desc_kmajor_sw128(a_addr + k * 32),
-                                  ptx::desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
-          const uint32_t e = ptx::smem_u32(&empty[stage]);
-          ptx::umma_commit_pair(ptx::mapa_shared(e, 0));
-          ptx::umma_commit_pair(ptx::mapa_shared(e, 1));
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint32_t off_a = uint32_t((k >> 2) * S::kAHalf + (k & 3) * 32);
+            const uint32_t off_b = uint32_t((k >> 2) * S::kBHalf + (k & 3) * 32);
+            ptx::umma_f16_ss_pair(d_tmem, ptx::desc_kmajor_sw128(a_addr + off_a),
+                                  ptx::desc_kmajor_sw128(b_addr + off_b), idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          ptx::umma_commit_pair_mc(&empty[stage], 0x3);  // frees the slot in both CTAs
           if (++stage == S::kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        const uint32_t f = ptx::smem_u32(&tfull[acc]);
-        ptx::umma_commit_pair(ptx::mapa_shared(f, 0));
-        ptx::umma_commit_pair(ptx::mapa_shared(f, 1));
+        ptx::umma_commit_pair_mc(&tfull[acc], 0x3);
       }
       ptx::umma_commit_pair(ptx::mapa_shared(ptx::smem_u32(drain), 0));
       const unsigned long long t0 = ptx::globaltimer();

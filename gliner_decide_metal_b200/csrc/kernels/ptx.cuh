@@ -294,6 +294,15 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t mbar_cluster_addr) {
                : "memory");
 }
 
+// One commit whose arrival lands on the mbarrier at the same shared-memory offset in every
+// CTA of `cta_mask` (both CTAs of the pair for 0b11) once this thread's prior pair MMAs
+// complete. (tcgen05.commit multicast: an arrive, not a data load.)
+__device__ __forceinline__ void umma_commit_pair_mc(uint64_t* local_bar, uint16_t cta_mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               ::"r"(smem_u32(local_bar)), "h"(cta_mask)
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
                "r"(ncols)

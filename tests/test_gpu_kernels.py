@@ -56,7 +56,8 @@ def _check(st):
 
 @pytest.mark.parametrize("M,N,K,act", [
     (128, 256, 64, 0), (1, 128, 64, 0), (5, 2048, 1024, 2), (300, 384, 1024, 1), (1000, 3072, 1024, 0),
-    (777, 1024, 4096, 0), (8192, 4096, 1024, 1), (8192, 1024, 4096, 0), (129, 256, 128, 2)])
+    (777, 1024, 4096, 0), (8192, 4096, 1024, 1), (8192, 1024, 4096, 0), (129, 256, 128, 2), (300, 256, 192, 0),
+    (4096, 3072, 1088, 0)])
 def test_linear_matches_numpy(M, N, K, act):
     """tcgen05 GEMM: out = act(a . w^T + b) vs float64 numpy on the same fp16 inputs."""
     torch = _torch()
