@@ -73,3 +73,27 @@ def test_config4_full_size_properties(weights_file):
                      c4.marker_mask[200:201])
     np.testing.assert_allclose(full[200:201], ref, atol=LOGIT_ATOL, rtol=0)
     model.close()
+
+
+def test_benchcli_batch_and_latency_modes(weights_file, tmp_path, capsys):
+    """The main.swift mirror: batch mode with a padded last chunk returns every row's logits
+    bit-identical to one classify of all rows; latency mode reports p50 / p95 / profile."""
+    import gliner_decide_metal_b200 as g
+    from conftest import load_golden
+    from gliner_decide_metal_b200 import benchcli
+    from gliner_decide_metal_b200.safetensors_io import load_file
+    path, _ = weights_file(7, 2, 1000)
+    gld = load_golden("ragged_B3_L40_2L")
+    inp = g.DecisionInput(gld["input_ids"], gld["attention_mask"], gld["marker_indices"], gld["marker_mask"])
+    inp.save(tmp_path / "in.safetensors")
+    common = ["--weights", str(path), "--inputs", str(tmp_path / "in.safetensors"), "--layers", "2", "--vocab", "1000"]
+    assert benchcli.main(common + ["--batch-size", "2", "--pad-batch", "--output", str(tmp_path / "b.safetensors")]) == 0
+    out = capsys.readouterr().out
+    assert "batch_count: 3" in out and "batch_rows_per_sec" in out
+    with g.GLiNERDecideClassifier(path, configuration=g.DeBERTaV2Configuration(num_hidden_layers=2,
+                                                                               vocab_size=1000)) as m:
+        want = m.classify(inp).logits
+    assert np.array_equal(load_file(tmp_path / "b.safetensors")["logits"], want)
+    assert benchcli.main(common + ["--iterations", "5", "--warmup", "1", "--profile"]) == 0
+    out = capsys.readouterr().out
+    assert "p50_ms" in out and "p95_ms" in out and "layer_1_feed_forward" in out
