@@ -11,11 +11,15 @@ Two modes, as there:
   and ``batch_rows_per_sec``.
 
 ``--output`` saves the logits (the last run's in latency mode, all rows in batch mode) to a
-safetensors file under the key ``logits``, as the reference does.
+safetensors file under the key ``logits``, as the reference does. Without the reference's
+checkpoint and sample inputs, ``--synthetic config0|config2|config4`` builds the BASELINE
+configuration's seeded input and ``--write-weights`` creates seeded random weights at the
+``--weights`` path when the file does not exist.
 """
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 import time
 from typing import Tuple
@@ -80,8 +84,10 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="python -m gliner_decide_metal_b200.benchcli",
                                  description="latency / batch benchmark of the classifier (main.swift)")
     ap.add_argument("--weights", required=True)
-    ap.add_argument("--inputs", required=True, help="safetensors with input_ids, attention_mask, marker_indices, "
-                                                     "marker_mask")
+    src = ap.add_mutually_exclusive_group(required=True)
+    src.add_argument("--inputs", help="safetensors with input_ids, attention_mask, marker_indices, marker_mask")
+    src.add_argument("--synthetic", choices=("config0", "config2", "config4"), help="seeded BASELINE input")
+    ap.add_argument("--write-weights", action="store_true", help="create seeded weights if --weights is missing")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iterations", type=int, default=20)
     ap.add_argument("--profile", action="store_true")
@@ -93,10 +99,18 @@ def main(argv=None) -> int:
     ap.add_argument("--output", default=None)
     args = ap.parse_args(argv)
     cfg = DeBERTaV2Configuration(num_hidden_layers=args.layers, vocab_size=args.vocab)
-    inp = DecisionInput.from_url(args.inputs)
+    if args.write_weights and not os.path.exists(args.weights):
+        from . import synthetic
+        synthetic.write_weights(args.weights, seed=0, num_layers=args.layers, vocab=args.vocab)
+    if args.synthetic:
+        from . import synthetic
+        b = getattr(synthetic, args.synthetic)()
+        inp = DecisionInput(b.input_ids, b.attention_mask, b.marker_indices, b.marker_mask)
+    else:
+        inp = DecisionInput.from_url(args.inputs)
     with GLiNERDecideClassifier(args.weights, configuration=cfg, device=args.device) as model:
         print(f"weights: {args.weights}")
-        print(f"inputs: {args.inputs}")
+        print(f"inputs: {args.inputs or args.synthetic} {inp.shape}")
         if args.batch_size > 0:
             logits, ms = run_batch(model, inp, args.batch_size, args.pad_batch, args.warmup)
             count = inp.input_ids.shape[0]

@@ -21,7 +21,9 @@ JSONL input line::
 
 Output (``--output`` or stdout): the reference's JSON array
 ``[{"id", "predictions": [{"task", "labels", "probabilities"}], "preprocessingMilliseconds",
-"inferenceMilliseconds"}]``.
+"inferenceMilliseconds"}]``. ``--synthetic-rows N`` replaces ``--jsonl`` with N seeded rows
+of BASELINE config 3 (mixed buckets, 1-3 tasks of 2-12 labels, 30% multi-label); the total
+rows per second of the run go to stderr.
 """
 from __future__ import annotations
 
@@ -124,9 +126,22 @@ def run_examples(models, examples: Sequence[TokenizedExample], buckets=DEFAULT_B
     return results
 
 
+def synthetic_examples(n: int, buckets=DEFAULT_BUCKETS, seed: int = 4) -> List[TokenizedExample]:
+    """``n`` seeded BASELINE config 3 rows as tokenised examples."""
+    from . import synthetic
+    out = []
+    for i, (ids, markers, n_labels, ml) in enumerate(synthetic.mixed_rows(n, seed=seed, buckets=buckets)):
+        tasks = [DecisionTask(f"task{h}", tuple(f"label{j}" for j in range(k)), m)
+                 for h, (k, m) in enumerate(zip(n_labels, ml))]
+        out.append(TokenizedExample(f"row{i}", [int(x) for x in ids], tasks, [list(p) for p in markers]))
+    return out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="python -m gliner_decide_metal_b200.serve", description=__doc__.split("\n")[0])
-    ap.add_argument("--jsonl", required=True, help="pre-tokenised examples, one JSON object per line")
+    src = ap.add_mutually_exclusive_group(required=True)
+    src.add_argument("--jsonl", help="pre-tokenised examples, one JSON object per line")
+    src.add_argument("--synthetic-rows", type=int, help="seeded BASELINE config 3 rows instead of --jsonl")
     ap.add_argument("--weights", required=True, help="fp16 safetensors weights")
     ap.add_argument("--buckets", default=",".join(str(b) for b in DEFAULT_BUCKETS))
     ap.add_argument("--batch-size", type=int, default=32)
@@ -139,9 +154,14 @@ def main(argv=None) -> int:
     cfg = DeBERTaV2Configuration(num_hidden_layers=args.layers, vocab_size=args.vocab)
     models = [GLiNERDecideClassifier(args.weights, configuration=cfg, device=int(d)) for d in args.devices.split(",")]
     try:
-        examples = load_jsonl(args.jsonl)
+        examples = load_jsonl(args.jsonl) if args.jsonl else synthetic_examples(args.synthetic_rows, buckets)
         print(f"loaded {len(examples)} examples", file=sys.stderr)
+        run_examples(models, examples[:min(len(examples), args.batch_size)], buckets, args.batch_size)  # warm-up
+        t0 = time.perf_counter()
         results = run_examples(models, examples, buckets, args.batch_size)
+        dt = time.perf_counter() - t0
+        print(f"rows: {len(examples)} total_ms: {dt * 1e3:.1f} rows_per_sec: {len(examples) / dt:.1f}",
+              file=sys.stderr)
     finally:
         for m in models:
             m.close()
