@@ -17,6 +17,13 @@ Printed JSON line (rank 0):
             peak in MEASURED_PEAKS.json
   cpu_baseline  the CPU restatement of the reference forward (oracle/, numpy fp32 BLAS,
             all host threads) on a bounded sample of the same workload (rank 0, N=1)
+  dense_grid  the same K steps with row packing off (every one of the B x L positions
+            through the encoder, as the reference computes them); the logits are
+            bit-identical, only the padding rows' work differs
+
+Row packing: each batch row's positions up to its last valid token (or active marker)
+are packed back to back and only those rows go through the encoder kernels; roofline
+FLOPs and bytes count the packed rows.
 
 ``--impl reference`` times that CPU restatement alone (the reference itself is Swift/MLX
 for Apple silicon and cannot run here) and prints its line with ``"impl": "reference"``.
@@ -52,7 +59,8 @@ GEMM_FLOPS_PER_TOKEN = 2 * (3 * HIDDEN * HIDDEN + HIDDEN * HIDDEN + 2 * HIDDEN *
 # and the weights + biases once
 GEMM_BYTES_PER_TOKEN = 2 * ((HIDDEN + 3 * HIDDEN) + (HIDDEN + HIDDEN) + (HIDDEN + INTER) + (INTER + HIDDEN))
 GEMM_WEIGHT_BYTES = 2 * (3 * HIDDEN * HIDDEN + HIDDEN * HIDDEN + 2 * HIDDEN * INTER + 5 * HIDDEN + INTER)
-ATTN_FLOPS_PER_SEQ = LAYERS * 16 * 4 * 2 * SEQ * SEQ * 64  # QK, c2p, p2c, PV as gathered dots
+# QK, c2p, p2c, PV as gathered dots, per (query, key) pair of one layer's 16 heads
+ATTN_FLOPS_PER_PAIR = LAYERS * 16 * 4 * 2 * 64
 
 
 def parse():
@@ -64,6 +72,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     ap.add_argument("--weights", type=str, default=None, help="reuse an existing weights file")
+    ap.add_argument("--no-dense-leg", action="store_true", help="skip the dense-grid comparison run")
     return ap.parse_args()
 
 
@@ -265,6 +274,11 @@ def main():
             mi=torch.from_numpy(b.marker_indices.astype(np.int32)).cuda(local),
             mm=torch.from_numpy(b.marker_mask.astype(np.float32)).cuda(local)))
     hm, o = batches[0].marker_indices.shape[1:]
+    # Packed encoder rows per batch (the extent rule of csrc/kernels/pack.cu): the GEMM and
+    # attention work the forward actually has to do.
+    layouts = [g.packed_row_layout(b.attention_mask, b.marker_indices, b.marker_mask) for b in batches]
+    packed_rows = [int(off[-1]) for _, off in layouts]
+    attn_pairs = [int((ext.astype(np.int64) ** 2).sum()) for ext, _ in layouts]
     logits = torch.empty((BATCH, hm, o), dtype=torch.float32, device=f"cuda:{local}")
     torch.cuda.synchronize(local)
 
@@ -326,6 +340,20 @@ def main():
     seqs = BATCH * args.steps * world
     value = seqs / (ms_max / 1e3)
 
+    # ---- the same steps on the dense [B, L] grid (the reference's layout), for comparison
+    dense = None
+    if not args.no_dense_leg:
+        model.row_packing = False
+        for i in range(3):
+            step(i)
+        ms_dense = max_over_ranks(timed_region(False))
+        model.check_errors()
+        model.row_packing = True
+        for i in range(3):
+            step(i)
+        dense = {"value": seqs / (ms_dense / 1e3), "ms_per_step": ms_dense / args.steps,
+                 "rows_per_step": BATCH * SEQ}
+
     # ---- e2e through the public API with host buffers
     host_inputs = [g.DecisionInput(b.input_ids, b.attention_mask, b.marker_indices, b.marker_mask) for b in batches]
     for i in range(2):
@@ -346,7 +374,8 @@ def main():
     gemm_names = ("qkv_gemm", "out_gemm", "ffn_up_gemm", "ffn_down_gemm")
     gemm_ns = sum(prof.get(n, (0, 0))[0] for n in gemm_names)
     gemm_launches = sum(prof.get(n, (0, 0))[1] for n in gemm_names)
-    gemm_flops = GEMM_FLOPS_PER_TOKEN * BATCH * SEQ * args.steps
+    rows_timed = sum(packed_rows[i % N_RESIDENT_BATCHES] for i in range(args.steps))
+    gemm_flops = GEMM_FLOPS_PER_TOKEN * rows_timed
     achieved_tflops = gemm_flops / (gemm_ns * 1e-9) / 1e12 if gemm_ns else None
     kernel_share = {k: round(v[0] / max(1, sum(x[0] for x in prof.values())), 4) for k, v in prof.items()}
     kernel_ms_per_step = {k: round(v[0] / 1e6 / args.steps, 4) for k, v in prof.items()}
@@ -367,13 +396,16 @@ def main():
                 "traffic": traffic,
                 "traffic_source": "profiles/gemm_traffic.json: ncu dram__bytes_read.sum + dram__bytes_write.sum per "
                                   "launch, layer-0 projections of this workload averaged",
-                "algorithmic_bytes_per_launch_avg": GEMM_BYTES_PER_TOKEN * BATCH * SEQ / 4 + GEMM_WEIGHT_BYTES / 4,
+                "algorithmic_bytes_per_launch_avg": GEMM_BYTES_PER_TOKEN * rows_timed / args.steps / 4
+                + GEMM_WEIGHT_BYTES / 4,
+                "algorithmic_units": f"{rows_timed / args.steps:.1f} packed rows per step (of {BATCH * SEQ} dense)",
                 "launches": gemm_launches,
                 "flops_per_launch_avg": gemm_flops / max(1, gemm_launches),
                 "kernel_ms_per_step": kernel_ms_per_step, "kernel_share": kernel_share}
     attn_ns = prof.get("attention", (0, 0))[0]
     if attn_ns:
-        roofline["attention_tflops"] = ATTN_FLOPS_PER_SEQ * BATCH * args.steps / (attn_ns * 1e-9) / 1e12
+        pairs = sum(attn_pairs[i % N_RESIDENT_BATCHES] for i in range(args.steps))
+        roofline["attention_tflops"] = ATTN_FLOPS_PER_PAIR * pairs / (attn_ns * 1e-9) / 1e12
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -382,7 +414,7 @@ def main():
                "sample": f"{rows} rows of the b32 L256 batch, one 24-layer fp32 forward per row, {dt:.1f} s "
                          "(oracle/reference_forward.py, numpy BLAS)"}
 
-    launches_per_step = 1 + LAYERS * 7 + 3
+    launches_per_step = 2 + LAYERS * 7 + 3  # row pack, embedding, 7 per layer, classifier
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -392,11 +424,15 @@ def main():
                                        "N(0,0.02) fp16 weights",
                            "batch_per_gpu": BATCH, "seq_len": SEQ, "parallelism": f"rows x{world} (no collective)",
                            "resident_batches": N_RESIDENT_BATCHES,
+                           "rows": "packed: each batch row's positions up to its last valid token run through "
+                                   "the encoder (logits bit-identical to the dense grid); "
+                                   f"{rows_timed / args.steps:.0f} of {BATCH * SEQ} rows per step",
                            "l2": "no flush: each step streams 0.87 GB of weights (> 126 MB L2) and cycles "
                                  f"{N_RESIDENT_BATCHES} distinct input batches"},
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "api": "gdc_classify (host numpy int64 ids / fp16 mask / int64 markers / fp32 marker mask)"},
                 "gpu_launches": launches_per_step * args.steps,
+                "dense_grid": dense,
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clk}
         print(json.dumps(line), flush=True)
     model.close()

@@ -33,7 +33,7 @@ from ._lib import (GDC_FLOAT16, GDC_FLOAT32, GDC_INT32, GDC_INT64, GDC_UINT8, ST
 __all__ = [
     "DeBERTaV2Configuration", "DecisionInput", "DecisionTask", "ProfileEvent", "InferenceResult", "Prediction",
     "GLiNERDecideClassifier", "make_input_from_tokens", "select_bucket", "decode", "decode_batch",
-    "classify_sharded", "relative_index_table", "GDCError", "MissingWeightError", "InvalidShapeError",
+    "classify_sharded", "relative_index_table", "packed_row_layout", "GDCError", "MissingWeightError", "InvalidShapeError",
     "InvalidInputError", "InputDoesNotFitError", "NoTaskLabelsError", "DEFAULT_BUCKETS",
 ]
 
@@ -255,6 +255,17 @@ class GLiNERDecideClassifier:
     def stream(self) -> int:
         return lib.gdc_model_stream(self._h) or 0
 
+    @property
+    def row_packing(self) -> bool:
+        """Packed encoder rows (only each batch row's positions up to its last valid token or
+        active marker run through the encoder) or the reference's dense [B, L] grid; the
+        logits are bit-identical. On by default."""
+        return bool(lib.gdc_model_row_packing(self._h))
+
+    @row_packing.setter
+    def row_packing(self, on: bool):
+        _check(lib.gdc_model_set_row_packing(self._h, int(bool(on))))
+
     def close(self):
         if getattr(self, "_h", None):
             lib.gdc_model_free(self._h)
@@ -398,6 +409,30 @@ def decode(logits: np.ndarray, tasks: Sequence[DecisionTask], row: int = 0):
         n = len(t.labels)
         out.append(Prediction(t.name, [t.labels[i] for i in range(n) if sel[0, h, i]], probs[0, h, :n].tolist()))
     return out
+
+
+def packed_row_layout(attention_mask: np.ndarray, marker_indices: np.ndarray, marker_mask: np.ndarray):
+    """Host statement of the packed-row layout the device computes (``csrc/kernels/pack.cu``):
+    per batch row the extent ``ext`` = 1 + max(last position with mask > 0, last marker index
+    with marker_mask > 0 inside [0, L)), or L for a row with no position of mask > 0, and the
+    offsets ``seq_off`` = [0, cumsum(ext)]; ``seq_off[-1]`` is the encoder's packed row count.
+    Returns (ext int32 [B], seq_off int64 [B + 1])."""
+    mask = np.asarray(attention_mask)
+    B, L = mask.shape
+    idx = np.asarray(marker_indices).reshape(B, -1)
+    act = np.asarray(marker_mask).reshape(B, -1) > 0
+    ext = np.empty(B, np.int32)
+    for b in range(B):
+        valid = np.nonzero(mask[b].astype(np.float32) > 0)[0]
+        if valid.size == 0:
+            ext[b] = L
+            continue
+        e = int(valid[-1]) + 1
+        mk = idx[b][act[b] & (idx[b] >= 0) & (idx[b] < L)]
+        if mk.size:
+            e = max(e, int(mk.max()) + 1)
+        ext[b] = e
+    return ext, np.concatenate([[0], np.cumsum(ext, dtype=np.int64)])
 
 
 def relative_index_table() -> np.ndarray:

@@ -60,6 +60,8 @@ SIGNATURES = [
     ("gdc_classify_device", C.c_int, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     ("gdc_check_errors", C.c_int, [_vp]),
     ("gdc_model_stream", _vp, [_vp]),
+    ("gdc_model_set_row_packing", C.c_int, [_vp, C.c_int]),
+    ("gdc_model_row_packing", C.c_int, [_vp]),
     ("gdc_profile_enable", C.c_int, [_vp, C.c_int]),
     ("gdc_profile_reset", C.c_int, [_vp]),
     ("gdc_profile_read", C.c_int, [_vp, C.POINTER(GdcProfileEvent), C.c_int, _pi32]),

@@ -289,6 +289,16 @@ gdc_status gdc_check_errors(gdc_model* m) {
   return read_device_errors(m, m->stream);
 }
 
+gdc_status gdc_model_set_row_packing(gdc_model* m, int enabled) {
+  if (!m) return set_error(GDC_ERR_NULL_POINTER, "null model");
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  set_row_packing(m, enabled != 0);
+  return GDC_OK;
+}
+
+int gdc_model_row_packing(const gdc_model* m) { return m && m->pack_rows ? 1 : 0; }
+
 gdc_status gdc_profile_enable(gdc_model* m, int enabled) {
   if (!m) return set_error(GDC_ERR_NULL_POINTER, "null model");
   std::lock_guard<std::mutex> lk(m->mu);

@@ -26,10 +26,12 @@ gdc_status launch_attention_simt(const __half* qkv, const __half* pos_qk, const 
 
 gdc_status launch_attention(const __half* qkv, const __half* pos_qk, const __half* key_mask,
                             const int32_t* rel_table, __half* ctx, int batch, int seq_len, int heads,
-                            cudaStream_t stream, int* err) {
+                            cudaStream_t stream, int* err, const AttentionWork& work) {
   if (batch <= 0 || seq_len <= 0) return GDC_OK;
   if (seq_len > 512) return set_error(GDC_ERR_UNSUPPORTED, "attention: seq_len %d > 512", seq_len);
   if (heads <= 0 || heads > 64) return set_error(GDC_ERR_UNSUPPORTED, "attention: heads %d", heads);
+  if (work.row_order != nullptr && (work.groups == nullptr || work.counter == nullptr || work.seq_off == nullptr))
+    return set_error(GDC_ERR_INVALID_INPUT, "attention: a row order needs groups, packed rows and a counter");
   if ((reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(pos_qk) & 15) ||
       (reinterpret_cast<uintptr_t>(ctx) & 15))
     return set_error(GDC_ERR_INVALID_INPUT, "attention: buffers must be 16-byte aligned");
@@ -52,7 +54,8 @@ gdc_status launch_attention(const __half* qkv, const __half* pos_qk, const __hal
   const int sms = device_sm_count(dev);
   const int grid = items < sms ? int(items) : sms;  // persistent: one CTA per SM
   attn::attention_tc_kernel<<<grid, attn::kThreads, attn::kSmemBytes, stream>>>(tm_qkv, tm_pos, key_mask, rel_table,
-                                                                                ctx, batch, seq_len, heads, err);
+                                                                                ctx, batch, seq_len, heads, err,
+                                                                                work);
   return check_launch("attention_tc_kernel");
 }
 

@@ -33,6 +33,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include "kernels.h"
 #include "ptx.cuh"
 
 namespace gdc {
@@ -63,7 +64,7 @@ constexpr int kOffTab = kOffC + 65536;         // relative index table, 1024 x i
 constexpr int kOffAdd = kOffTab + 2048;        // per key of the tile: 0 valid, -65504 masked, -inf beyond L
 constexpr int kOffRed = kOffAdd + 512;         // cross-part max exchange, 4 x 128 f32
 constexpr int kOffRedL = kOffRed + 2048;       // cross-part denominator exchange, 4 x 128 f32
-constexpr int kOffFlags = kOffRedL + 2048;     // per item (2 slots): processed-key-tile mask
+constexpr int kOffFlags = kOffRedL + 2048;     // per item (2 slots): key-tile mask, then item index
 constexpr int kOffBar = kOffFlags + 64;        // mbarriers
 constexpr int kNumBars = 14;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
@@ -184,6 +185,14 @@ __device__ __forceinline__ uint32_t key_tile_mask(const MaskChunk& c, int n_kt) 
   return m != 0 ? m : ((1u << n_kt) - 1u);
 }
 
+// Work distribution of a launch. Without a counter every CTA takes every gridDim.x-th
+// item. With one, CTAs take items one at a time from a shared atomic counter (reset to zero
+// by the last CTA to finish); with row_order / groups (packed rows) the counter's values
+// map to the live items heaviest first: rows grouped by their number of key tiles c
+// (groups[c] rows each, row_order lists them by descending c), each row's items ordered
+// (query tile, head). An item costs up to c pairs, so the cheap items come last.
+using Schedule = ::gdc::AttentionWork;
+
 __device__ __forceinline__ int next_tile(uint32_t mask, int kt) {
   const uint32_t rest = kt < 0 ? mask : mask & ~((2u << kt) - 1u);  // tiles after kt
   return rest ? __ffs(int(rest)) - 1 : -1;
@@ -194,7 +203,7 @@ __device__ __forceinline__ int next_tile(uint32_t mask, int kt) {
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_pos,
                         const __half* __restrict__ key_mask, const int32_t* __restrict__ rel_table,
-                        __half* __restrict__ ctx, int B, int L, int heads, int* err) {
+                        __half* __restrict__ ctx, int B, int L, int heads, int* err, const Schedule sc) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   int16_t* s_tab = reinterpret_cast<int16_t*>(sm + kOffTab);
@@ -202,6 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* s_red = reinterpret_cast<float*>(sm + kOffRed);
   float* s_red_l = reinterpret_cast<float*>(sm + kOffRedL);
   volatile uint32_t* s_flags = reinterpret_cast<volatile uint32_t*>(sm + kOffFlags);
+  volatile int32_t* s_item = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 16);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffTmemSlot);
 
@@ -233,6 +243,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lo = s_tab[q0 - (k0 + kTile - 1) + 511];
     return lo < 512 - kWin ? lo : 512 - kWin;
   };
+  // Packed rows (sc.seq_off != null): batch row b occupies qkv / ctx rows [seq_off[b],
+  // seq_off[b+1]); positions at or past its extent are not computed and items whose query
+  // tile starts past the extent are never handed out. The producer picks the items and
+  // publishes each one (s_item) to the MMA issuer and the row warps.
+  const int32_t* __restrict__ seq_off = sc.seq_off;
+  auto row_base = [&](int b) -> int { return seq_off != nullptr ? seq_off[b] : b * L; };
+  auto extent = [&](int b) -> int { return seq_off != nullptr ? seq_off[b + 1] - seq_off[b] : L; };
+  auto next_live = [&](int item) {
+    if (seq_off != nullptr) {
+      while (item < n_items) {
+        const Item x = decode_item(item, n_kt, heads);
+        if (x.qt * kTile < extent(x.b)) break;
+        item += int(gridDim.x);
+      }
+    }
+    return item;
+  };
+  // counter value j -> item, or -1 past the last one
+  auto map_item = [&](int j) -> int {
+    if (sc.row_order == nullptr) return j < n_items ? j : -1;
+    int row = 0;
+    for (int c = n_kt; c >= 1; --c) {
+      const int rows_c = sc.groups[c];
+      const int per_row = c * heads;
+      if (j < rows_c * per_row) {
+        const int r = j / per_row;
+        const int rem = j - r * per_row;
+        const int b = sc.row_order[row + r];
+        return (b * heads + rem % heads) * n_kt + rem / heads;
+      }
+      j -= rows_c * per_row;
+      row += rows_c;
+    }
+    return -1;
+  };
 
   if (warp == kRowWarps + 1) {
     // ------------------------------------------------------------ TMA producer warp
@@ -248,13 +293,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::prefetch_tensor_map(&tm_qkv);
       ptx::prefetch_tensor_map(&tm_pos);
     }
-    int item = blockIdx.x, item_idx = 0, kt = -1, np = 0, loads_issued = 0, q_issued = 0;
+    int cursor = int(blockIdx.x);  // static distribution: next candidate item (lane 0)
+    auto fetch = [&]() -> int {
+      int v = -1;
+      if (lane == 0) {
+        if (sc.counter == nullptr) {
+          const int x = next_live(cursor);
+          cursor = x + int(gridDim.x);
+          v = x < n_items ? x : -1;
+        } else {
+          v = map_item(atomicAdd(sc.counter, 1));
+        }
+      }
+      return __shfl_sync(0xffffffffu, v, 0);
+    };
+    int item = fetch(), item_idx = 0, kt = -1, np = 0, loads_issued = 0, q_issued = 0;
     uint32_t tmask = 0;
     Item it{};
     MaskChunk pre{};  // key-mask registers prefetched for the upcoming item (batch row pre_b)
     int pre_b = -1;
     bool ok = true;
-    while (item < n_items) {
+    while (item >= 0) {
       // pair np is the first of item `item`: publish its tile mask and load Q
       it = decode_item(item, n_kt, heads);
       if (pre_b != it.b) {
@@ -262,14 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         pre_b = it.b;
       }
       tmask = key_tile_mask(pre, n_kt);
-      const int nxt = item + int(gridDim.x);
-      if (nxt < n_items) {
-        const int nb = decode_item(nxt, n_kt, heads).b;
-        if (nb != pre_b) {
-          pre = load_mask_chunk(key_mask, (long long)nb * L, L);  // consumed at the next item
-          pre_b = nb;
-        }
-      }
+      int nxt = -1;
       bool first = true;
       for (kt = next_tile(tmask, -1); kt >= 0; kt = next_tile(tmask, kt)) {
         if (lane == 0 && np > 0) {
@@ -284,14 +336,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           if (first) {
             s_flags[item_idx & 1] = tmask;
-            ptx::mbar_arrive(&bars[kBarFlags]);  // release: the mask is visible to the consumers
+            s_item[item_idx & 1] = item;
+            ptx::mbar_arrive(&bars[kBarFlags]);  // release: mask and item are visible to the consumers
             ptx::mbar_arrive_expect_tx(&bars[kBarQ], 16384);
-            ptx::tma_load_2d(sQ, &tm_qkv, it.h * 64, it.b * L + it.qt * kTile, &bars[kBarQ]);
+            ptx::tma_load_2d(sQ, &tm_qkv, it.h * 64, row_base(it.b) + it.qt * kTile, &bars[kBarQ]);
           }
           const int buf = np & 1;
           const int k0 = kt * kTile;
           const int lo = window_lo(it.qt * kTile, k0);
-          const int krow = it.b * L + k0;
+          const int krow = row_base(it.b) + k0;
           uint64_t* bar = &bars[kBarKV0 + buf];
           ptx::mbar_arrive_expect_tx(bar, 2 * 16384 + 2 * 32768);
           ptx::tma_load_2d(sm + kOffK + buf * 16384, &tm_qkv, E + it.h * 64, krow, bar);
@@ -299,14 +352,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tma_load_2d(sPK, &tm_pos, E + it.h * 64, lo, bar);
           ptx::tma_load_2d(sPQ, &tm_pos, it.h * 64, lo, bar);
         }
-        if (first) ++q_issued;
+        if (first) {
+          ++q_issued;
+          // the next item, fetched while this pair computes, and its key-mask registers
+          nxt = fetch();
+          if (nxt >= 0) {
+            const int nb = decode_item(nxt, n_kt, heads).b;
+            if (nb != pre_b) {
+              pre = load_mask_chunk(key_mask, (long long)nb * L, L);  // consumed at the next item
+              pre_b = nb;
+            }
+          }
+        }
         first = false;
         ++loads_issued;
         ++np;
       }
       if (!ok) break;
-      item += gridDim.x;
+      item = nxt;
       ++item_idx;
+    }
+    if (ok && lane == 0) {
+      // End of the work list: item -1. Published only after the last pair's gathers, so
+      // every consumer has already seen the previous publication (a barrier phase cannot
+      // complete twice ahead of a waiter).
+      if (np == 0 || ptx::mbar_wait_sleep(&bars[kBarProbs], uint32_t((np - 1) & 1), err)) {
+        s_flags[item_idx & 1] = 0;
+        s_item[item_idx & 1] = -1;
+        ptx::mbar_arrive(&bars[kBarFlags]);
+      }
     }
     if (lane == 0) {
       // wait (bounded) for the last issued loads to land before the CTA can exit
@@ -333,8 +407,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t aPQ = ptx::smem_u32(sm + kOffW + 32768), aProb = ptx::smem_u32(sm + kOffC);
       int np = 0, item_idx = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_idx) {
+      for (; ok; ++item_idx) {
         if (!ptx::mbar_wait(&bars[kBarFlags], uint32_t(item_idx & 1), err)) break;
+        if (s_item[item_idx & 1] < 0) break;
         const uint32_t tmask = s_flags[item_idx & 1];
         bool first = true;
         for (int kt = next_tile(tmask, -1); kt >= 0; kt = next_tile(tmask, kt), ++np) {
@@ -399,16 +474,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     int np = 0;
     int item_idx = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_idx) {
-      const Item it = decode_item(item, n_kt, heads);
-      const int q0 = it.qt * kTile;
-      const int q = q0 + t;
-      const long long row0 = (long long)it.b * L;
+    for (; ok; ++item_idx) {
       if (!ptx::mbar_wait_sleep(&bars[kBarFlags], uint32_t(item_idx & 1), err)) {
         ok = false;
         break;
       }
+      const int item = s_item[item_idx & 1];
+      if (item < 0) break;
       const uint32_t tmask = s_flags[item_idx & 1];
+      const Item it = decode_item(item, n_kt, heads);
+      const int q0 = it.qt * kTile;
+      const int q = q0 + t;
+      const long long row0 = (long long)it.b * L;  // key mask row ([B, L] in both layouts)
+      const long long orow0 = row_base(it.b);     // qkv / ctx row of position 0
+      const int ext = extent(it.b);
       float m_run = -INFINITY, l_part = 0.f;
       bool first_pair = true;
       for (int kt = next_tile(tmask, -1); kt >= 0; kt = next_tile(tmask, kt), ++np) {
@@ -417,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t par = uint32_t(np & 1);
         if (part == 0) {
           const int k = k0 + t;
-          s_add[t] = k >= L ? -INFINITY : (__half2float(key_mask[row0 + k]) > 0.f ? 0.f : -65504.0f);
+          s_add[t] = k >= ext ? -INFINITY : (__half2float(key_mask[row0 + k]) > 0.f ? 0.f : -65504.0f);
         }
         // ---- drain C (own query row, this part's 64 columns)
         if (!ptx::mbar_wait_sleep(&bars[kBarSC], par, err)) {
@@ -554,12 +633,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      if (q < L) {
+      if (q < ext) {
         float lsum = s_red_l[t];
 #pragma unroll
         for (int pp = 1; pp < kParts; ++pp) lsum += s_red_l[pp * 128 + t];
         const float inv = 1.0f / lsum;
-        __half* dst = ctx + (row0 + q) * (long long)E + it.h * 64 + part * kOPP;
+        __half* dst = ctx + (orow0 + q) * (long long)E + it.h * 64 + part * kOPP;
 #pragma unroll
         for (int c = 0; c < kOPP / 8; ++c) {
           uint4 v;
@@ -577,6 +656,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kRowWarps) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tbase, kTmemCols);
+  }
+  if (sc.counter != nullptr && threadIdx.x == 0) {
+    // every fetch of this CTA has completed (its producer saw the end of the list)
+    __threadfence();
+    if (atomicAdd(sc.counter + 1, 1) == int(gridDim.x) - 1) {
+      atomicExch(sc.counter, 0);
+      atomicExch(sc.counter + 1, 0);
+    }
   }
 }
 

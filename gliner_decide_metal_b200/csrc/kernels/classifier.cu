@@ -14,7 +14,7 @@ namespace {
 
 __global__ void marker_gather_kernel(const __half* __restrict__ hidden, const int32_t* __restrict__ markers,
                                      __half* __restrict__ rows, int n_rows, int per_batch, int seq_len, int cols,
-                                     int* err) {
+                                     int* err, const int32_t* __restrict__ seq_off) {
   const int r = blockIdx.x;
   if (r >= n_rows) return;
   const int b = r / per_batch;
@@ -23,7 +23,12 @@ __global__ void marker_gather_kernel(const __half* __restrict__ hidden, const in
     if (threadIdx.x == 0) atomicOr(err, kErrBadMarkerIndex);
     idx = 0;
   }
-  const uint4* src = reinterpret_cast<const uint4*>(hidden + ((long long)b * seq_len + idx) * cols);
+  long long row = (long long)b * seq_len + idx;
+  if (seq_off != nullptr) {
+    const int off = seq_off[b];
+    row = off + (idx < seq_off[b + 1] - off ? idx : 0);  // an inactive marker past the extent
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(hidden + row * cols);
   uint4* dst = reinterpret_cast<uint4*>(rows + (long long)r * cols);
   for (int i = threadIdx.x; i < cols / 8; i += blockDim.x) dst[i] = src[i];
 }
@@ -108,10 +113,11 @@ __global__ void decode_kernel(const float* __restrict__ logits, int batch, int m
 }  // namespace
 
 gdc_status launch_marker_gather(const __half* hidden, const int32_t* markers, __half* rows, int n_rows, int per_batch,
-                                int seq_len, int cols, cudaStream_t stream, int* err) {
+                                int seq_len, int cols, cudaStream_t stream, int* err, const int32_t* seq_off) {
   if (n_rows <= 0) return GDC_OK;
   if (cols % 8 != 0 || per_batch <= 0) return set_error(GDC_ERR_UNSUPPORTED, "marker gather: bad shape");
-  marker_gather_kernel<<<n_rows, 128, 0, stream>>>(hidden, markers, rows, n_rows, per_batch, seq_len, cols, err);
+  marker_gather_kernel<<<n_rows, 128, 0, stream>>>(hidden, markers, rows, n_rows, per_batch, seq_len, cols, err,
+                                                   seq_off);
   return check_launch("marker_gather_kernel");
 }
 

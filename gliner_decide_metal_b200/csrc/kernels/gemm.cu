@@ -62,9 +62,10 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + e
 template <int BN, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                   const __half* __restrict__ bias, __half* __restrict__ out, int M, int N, int K, long long ldo,
-                   int* err) {
+                   const __half* __restrict__ bias, __half* __restrict__ out, int M_cap, int N, int K, long long ldo,
+                   int* err, const int32_t* __restrict__ m_dev) {
   using S = GemmShape<BN>;
+  const int M = m_dev != nullptr ? min(M_cap, *m_dev) : M_cap;  // rows computed
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
@@ -265,7 +266,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int BN, int ACT>
 gdc_status launch_gemm_variant(const CUtensorMap& ta, const CUtensorMap& tw, const __half* bias, __half* out,
-                               long long ldo, int M, int N, int K, cudaStream_t stream, int* err) {
+                               long long ldo, int M, int N, int K, cudaStream_t stream, int* err,
+                               const int32_t* m_dev) {
   using S = GemmShape<BN>;
   auto kern = gemm_tn_kernel<BN, ACT>;
   static bool configured[64] = {};
@@ -278,7 +280,7 @@ gdc_status launch_gemm_variant(const CUtensorMap& ta, const CUtensorMap& tw, con
   }
   const int num_tiles = ((M + kBM - 1) / kBM) * (N / BN);
   const int grid = num_tiles < device_sm_count(dev) ? num_tiles : device_sm_count(dev);
-  kern<<<grid, kThreads, S::kSmemBytes, stream>>>(ta, tw, bias, out, M, N, K, ldo, err);
+  kern<<<grid, kThreads, S::kSmemBytes, stream>>>(ta, tw, bias, out, M, N, K, ldo, err, m_dev);
   return check_launch("gemm_tn_kernel");
 }
 
@@ -342,7 +344,8 @@ int device_sm_count(int device) {
 }
 
 gdc_status launch_linear(const __half* a, int64_t lda, const __half* w, const __half* bias, __half* out,
-                         int64_t ldo, int64_t M, int N, int K, int act, cudaStream_t stream, int* err) {
+                         int64_t ldo, int64_t M, int N, int K, int act, cudaStream_t stream, int* err,
+                         const int32_t* m_dev) {
   if (M <= 0) return GDC_OK;
   if (N <= 0 || K <= 0 || N % 128 != 0 || K % kBK != 0)
     return set_error(GDC_ERR_UNSUPPORTED, "linear: N=%d must be a multiple of 128 and K=%d of 64", N, K);
@@ -357,20 +360,21 @@ gdc_status launch_linear(const __half* a, int64_t lda, const __half* w, const __
     const char* e = std::getenv("GDC_GEMM_SINGLE_CTA");
     return e != nullptr && e[0] == '1';
   }();
-  if (M > 128 && !force_single) return launch_linear_pair(a, lda, w, bias, out, ldo, M, N, K, act, stream, err);
+  if (M > 128 && !force_single)
+    return launch_linear_pair(a, lda, w, bias, out, ldo, M, N, K, act, stream, err, m_dev);
   const int bn = (N % 256 == 0) ? 256 : 128;
   CUtensorMap ta, tw;
   GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), kBM));
   GDC_TRY(make_tmap_2d(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn)));
   const int m = int(M);
   if (bn == 256) {
-    if (act == kActGelu) return launch_gemm_variant<256, kActGelu>(ta, tw, bias, out, ldo, m, N, K, stream, err);
-    if (act == kActRelu) return launch_gemm_variant<256, kActRelu>(ta, tw, bias, out, ldo, m, N, K, stream, err);
-    return launch_gemm_variant<256, kActNone>(ta, tw, bias, out, ldo, m, N, K, stream, err);
+    if (act == kActGelu) return launch_gemm_variant<256, kActGelu>(ta, tw, bias, out, ldo, m, N, K, stream, err, m_dev);
+    if (act == kActRelu) return launch_gemm_variant<256, kActRelu>(ta, tw, bias, out, ldo, m, N, K, stream, err, m_dev);
+    return launch_gemm_variant<256, kActNone>(ta, tw, bias, out, ldo, m, N, K, stream, err, m_dev);
   }
-  if (act == kActGelu) return launch_gemm_variant<128, kActGelu>(ta, tw, bias, out, ldo, m, N, K, stream, err);
-  if (act == kActRelu) return launch_gemm_variant<128, kActRelu>(ta, tw, bias, out, ldo, m, N, K, stream, err);
-  return launch_gemm_variant<128, kActNone>(ta, tw, bias, out, ldo, m, N, K, stream, err);
+  if (act == kActGelu) return launch_gemm_variant<128, kActGelu>(ta, tw, bias, out, ldo, m, N, K, stream, err, m_dev);
+  if (act == kActRelu) return launch_gemm_variant<128, kActRelu>(ta, tw, bias, out, ldo, m, N, K, stream, err, m_dev);
+  return launch_gemm_variant<128, kActNone>(ta, tw, bias, out, ldo, m, N, K, stream, err, m_dev);
 }
 
 }  // namespace gdc

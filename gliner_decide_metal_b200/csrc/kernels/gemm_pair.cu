@@ -57,9 +57,10 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + e
 template <int BN, int ACT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                     const __grid_constant__ CUtensorMap tm_out, const __half* __restrict__ bias, int M, int N, int K,
-                     int* err) {
+                     const __grid_constant__ CUtensorMap tm_out, const __half* __restrict__ bias, int M_cap, int N,
+                     int K, int* err, const int32_t* __restrict__ m_dev) {
   using S = PairShape<BN>;
+  const int M = m_dev != nullptr ? min(M_cap, *m_dev) : M_cap;  // rows computed (same in both CTAs)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
@@ -277,7 +278,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 template <int BN, int ACT>
 gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const __half* bias,
-                               int M, int N, int K, cudaStream_t stream, int* err) {
+                               int M, int N, int K, cudaStream_t stream, int* err, const int32_t* m_dev) {
   using S = PairShape<BN>;
   auto kern = gemm_pair_kernel<BN, ACT>;
   static bool configured[64] = {};
@@ -291,7 +292,7 @@ gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, con
   const int num_tiles = ((M + 255) / 256) * (N / BN);
   const int pairs_avail = device_sm_count(dev) / 2;
   const int pairs = num_tiles < pairs_avail ? num_tiles : pairs_avail;
-  kern<<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(ta, tw, to, bias, M, N, K, err);
+  kern<<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(ta, tw, to, bias, M, N, K, err, m_dev);
   return check_launch("gemm_pair_kernel");
 }
 
@@ -316,7 +317,8 @@ int choose_bn(int64_t M, int N, int pairs) {
 }  // namespace
 
 gdc_status launch_linear_pair(const __half* a, int64_t lda, const __half* w, const __half* bias, __half* out,
-                              int64_t ldo, int64_t M, int N, int K, int act, cudaStream_t stream, int* err) {
+                              int64_t ldo, int64_t M, int N, int K, int act, cudaStream_t stream, int* err,
+                              const int32_t* m_dev) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int bn = choose_bn(M, N, device_sm_count(dev) / 2);
@@ -328,9 +330,9 @@ gdc_status launch_linear_pair(const __half* a, int64_t lda, const __half* w, con
   const int m = int(M);
 #define GDC_PAIR_CASE(BNV)                                                                              \
   if (bn == BNV) {                                                                                      \
-    if (act == kActGelu) return launch_pair_variant<BNV, kActGelu>(ta, tw, to, bias, m, N, K, stream, err); \
-    if (act == kActRelu) return launch_pair_variant<BNV, kActRelu>(ta, tw, to, bias, m, N, K, stream, err); \
-    return launch_pair_variant<BNV, kActNone>(ta, tw, to, bias, m, N, K, stream, err);          \
+    if (act == kActGelu) return launch_pair_variant<BNV, kActGelu>(ta, tw, to, bias, m, N, K, stream, err, m_dev); \
+    if (act == kActRelu) return launch_pair_variant<BNV, kActRelu>(ta, tw, to, bias, m, N, K, stream, err, m_dev); \
+    return launch_pair_variant<BNV, kActNone>(ta, tw, to, bias, m, N, K, stream, err, m_dev); \
   }
   GDC_PAIR_CASE(256)
   GDC_PAIR_CASE(192)

@@ -62,11 +62,12 @@ __device__ __forceinline__ void ln_row_store(float (&v)[CH * 8], const __half* _
 template <int CH>
 __global__ void __launch_bounds__(kRowsPerBlock * 32)
     residual_ln_kernel(const __half* __restrict__ x, const __half* __restrict__ res, const __half* __restrict__ gamma,
-                       const __half* __restrict__ beta, __half* __restrict__ out, long long rows, float eps) {
+                       const __half* __restrict__ beta, __half* __restrict__ out, long long rows, float eps,
+                       const int32_t* __restrict__ m_dev) {
   constexpr int cols = CH * 256;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  if (row >= rows || (m_dev != nullptr && row >= *m_dev)) return;
   const __half* xr = x + row * cols;
   float v[CH * 8];
 #pragma unroll
@@ -99,12 +100,14 @@ template <int CH>
 __global__ void __launch_bounds__(kRowsPerBlock * 32)
     embedding_kernel(const int32_t* __restrict__ ids, const __half* __restrict__ mask, const __half* __restrict__ table,
                      long long vocab, const __half* __restrict__ gamma, const __half* __restrict__ beta,
-                     __half* __restrict__ out, long long rows, float eps, int* err) {
+                     __half* __restrict__ out, long long rows, float eps, int* err,
+                     const int32_t* __restrict__ rowmap, const int32_t* __restrict__ m_dev) {
   constexpr int cols = CH * 256;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  long long id = ids[row];
+  if (row >= rows || (m_dev != nullptr && row >= *m_dev)) return;
+  const long long src = rowmap != nullptr ? (long long)rowmap[row] : row;  // dense position of the row
+  long long id = ids[src];
   if (id < 0 || id >= vocab) {
     if (lane == 0) atomicOr(err, kErrBadTokenId);
     id = 0;
@@ -123,7 +126,7 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
       v[c * 8 + 2 * j + 1] = s.y;
     }
   }
-  const float m = __half2float(mask[row]);
+  const float m = __half2float(mask[src]);
   // scale_after == 1 would skip the rounding; a mask of exactly 1 changes nothing anyway.
   ln_row_store<CH>(v, gamma, beta, out + row * cols, lane, eps, m);
 }
@@ -143,24 +146,27 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
 
 gdc_status launch_residual_layer_norm(const __half* x, const __half* residual, const __half* gamma,
                                       const __half* beta, __half* out, int64_t rows, int cols, float eps,
-                                      cudaStream_t stream) {
+                                      cudaStream_t stream, const int32_t* m_dev) {
   if (rows <= 0) return GDC_OK;
   if (cols <= 0 || cols % 256 != 0 || cols > 4096)
     return set_error(GDC_ERR_UNSUPPORTED, "layer norm: cols=%d must be a multiple of 256 and <= 4096", cols);
   const unsigned grid = unsigned((rows + kRowsPerBlock - 1) / kRowsPerBlock);
-  GDC_LN_DISPATCH(cols / 256, residual_ln_kernel, x, residual, gamma, beta, out, (long long)rows, eps);
+  GDC_LN_DISPATCH(cols / 256, residual_ln_kernel, x, residual, gamma, beta, out, (long long)rows, eps, m_dev);
   return check_launch("residual_ln_kernel");
 }
 
 gdc_status launch_embedding(const int32_t* ids, const __half* mask, const __half* table, int64_t vocab,
                             const __half* gamma, const __half* beta, __half* out, int64_t rows, int cols,
-                            float eps, cudaStream_t stream, int* err) {
+                            float eps, cudaStream_t stream, int* err, const int32_t* rowmap,
+                            const int32_t* m_dev) {
   if (rows <= 0) return GDC_OK;
   if (cols <= 0 || cols % 256 != 0 || cols > 4096)
     return set_error(GDC_ERR_UNSUPPORTED, "embedding: cols=%d unsupported", cols);
+  if ((rowmap == nullptr) != (m_dev == nullptr))
+    return set_error(GDC_ERR_INVALID_INPUT, "embedding: rowmap and row count go together");
   const unsigned grid = unsigned((rows + kRowsPerBlock - 1) / kRowsPerBlock);
   GDC_LN_DISPATCH(cols / 256, embedding_kernel, ids, mask, table, (long long)vocab, gamma, beta, out,
-                  (long long)rows, eps, err);
+                  (long long)rows, eps, err, rowmap, m_dev);
   return check_launch("embedding_kernel");
 }
 

@@ -93,6 +93,10 @@ gdc_status model_load(const char* path, const gdc_config* cfg_in, int device, gd
   m->layers_n = cfg.num_hidden_layers;
   m->vocab = cfg.vocab_size;
   m->eps = cfg.layer_norm_eps;
+  {
+    const char* v = std::getenv("GDC_PACK_ROWS");  // "0": dense rows by default
+    m->pack_rows = !(v && v[0] == '0');
+  }
   m->layers.resize(size_t(cfg.num_hidden_layers));
 
   std::vector<PendingUpload> ups;
@@ -266,8 +270,9 @@ void model_free(gdc_model* m) {
   if (m->stream) cudaStreamSynchronize(m->stream);
   Workspace& w = m->ws;
   for (void* p : {(void*)w.x, (void*)w.x1, (void*)w.big, (void*)w.ctx, (void*)w.tmp, (void*)w.mrows,
-                  (void*)w.mhid, (void*)w.ids, (void*)w.mask, (void*)w.marker_idx, (void*)w.marker_mask,
-                  (void*)w.logits, (void*)w.logits16})
+                  (void*)w.mhid, (void*)w.ids, (void*)w.mask, (void*)w.seq_off, (void*)w.rowmap,
+                  (void*)w.row_order, (void*)w.ctrl,
+                  (void*)w.marker_idx, (void*)w.marker_mask, (void*)w.logits, (void*)w.logits16})
     if (p) cudaFree(p);
   if (w.h_in) cudaFreeHost(w.h_in);
   if (w.h_out) cudaFreeHost(w.h_out);
@@ -304,6 +309,19 @@ gdc_status ensure_workspace(gdc_model* m, int64_t tokens, int64_t markers) {
     GDC_TRY(grow((void**)&w.tmp, size_t(cap) * E * 2));
     GDC_TRY(grow((void**)&w.ids, size_t(cap) * 4));
     GDC_TRY(grow((void**)&w.mask, size_t(cap) * 2));
+    GDC_TRY(grow((void**)&w.seq_off, size_t(cap + 1) * 4));
+    GDC_TRY(grow((void**)&w.rowmap, size_t(cap) * 4));
+    GDC_TRY(grow((void**)&w.row_order, size_t(cap) * 4));
+    if (!w.ctrl) GDC_TRY(grow((void**)&w.ctrl, 64 * 4));
+    GDC_CUDA_TRY(cudaMemsetAsync(w.ctrl, 0, 64 * 4, m->stream));
+    // With packed rows, GEMM tiles and attention key tiles also read rows past the packed
+    // count that no kernel of this call wrote. Starting every activation buffer at zero keeps
+    // such rows finite (later they hold finite values of earlier calls), so a masked key's
+    // zero probability never meets an Inf or NaN value row.
+    for (void* p : {(void*)w.x, (void*)w.x1, (void*)w.ctx, (void*)w.tmp})
+      GDC_CUDA_TRY(cudaMemsetAsync(p, 0, size_t(cap) * E * 2, m->stream));
+    GDC_CUDA_TRY(cudaMemsetAsync(w.big, 0, size_t(cap) * big_cols * 2, m->stream));
+    GDC_CUDA_TRY(cudaStreamSynchronize(m->stream));  // the forward may run on another stream
     w.tokens = cap;
     ++w.generation;
   }
@@ -361,28 +379,48 @@ gdc_status enqueue_forward(gdc_model* m, int B, int L, int Hm, int O, const int3
   const int64_t R = int64_t(B) * Hm * O;
   const int E = m->hidden, F = m->inter;
   Workspace& w = m->ws;
+  // Packed rows: seq_off / rowmap from the mask and markers on the device; every encoder
+  // kernel then reads the packed row count seq_off[B] (m_dev), the buffers keep their
+  // B * L capacity and the launch shapes stay those of the dense grid.
+  const int32_t* seq_off = nullptr;
+  const int32_t* rowmap = nullptr;
+  const int32_t* m_dev = nullptr;
+  // attention CTAs take work items from the workspace counter (heaviest first when packed)
+  AttentionWork work;
+  work.counter = w.ctrl;
   rec.begin();
-  GDC_TRY(launch_embedding(ids, mask, m->word_emb, m->vocab, m->emb_ln_g, m->emb_ln_b, w.x, T, E, m->eps, s, m->err));
+  if (m->pack_rows) {
+    GDC_TRY(launch_row_pack(mask, markers, marker_mask, B, L, Hm * O, w.seq_off, w.rowmap, w.row_order, w.ctrl + 8,
+                            s));
+    seq_off = w.seq_off;
+    rowmap = w.rowmap;
+    m_dev = w.seq_off + B;
+    work.seq_off = w.seq_off;
+    work.row_order = w.row_order;
+    work.groups = w.ctrl + 8;
+  }
+  GDC_TRY(launch_embedding(ids, mask, m->word_emb, m->vocab, m->emb_ln_g, m->emb_ln_b, w.x, T, E, m->eps, s, m->err,
+                           rowmap, m_dev));
   rec.end(kProfEmbedding, "embedding");
   for (int i = 0; i < m->layers_n; ++i) {
     const LayerWeights& Lw = m->layers[size_t(i)];
     const std::string p = rec.named ? "layer_" + std::to_string(i) + "_" : std::string();
-    GDC_TRY(launch_linear(w.x, E, Lw.wqkv, Lw.bqkv, w.big, 3 * E, T, 3 * E, E, kActNone, s, m->err));
+    GDC_TRY(launch_linear(w.x, E, Lw.wqkv, Lw.bqkv, w.big, 3 * E, T, 3 * E, E, kActNone, s, m->err, m_dev));
     rec.end(kProfQkvGemm, p + "attention_projection");
-    GDC_TRY(launch_attention(w.big, Lw.pos_qk, mask, m->rel_table, w.ctx, B, L, m->heads, s, m->err));
+    GDC_TRY(launch_attention(w.big, Lw.pos_qk, mask, m->rel_table, w.ctx, B, L, m->heads, s, m->err, work));
     rec.end(kProfAttention, p + "attention");
-    GDC_TRY(launch_linear(w.ctx, E, Lw.wo, Lw.bo, w.tmp, E, T, E, E, kActNone, s, m->err));
+    GDC_TRY(launch_linear(w.ctx, E, Lw.wo, Lw.bo, w.tmp, E, T, E, E, kActNone, s, m->err, m_dev));
     rec.end(kProfOutGemm, "");
-    GDC_TRY(launch_residual_layer_norm(w.tmp, w.x, Lw.ln1_g, Lw.ln1_b, w.x1, T, E, m->eps, s));
+    GDC_TRY(launch_residual_layer_norm(w.tmp, w.x, Lw.ln1_g, Lw.ln1_b, w.x1, T, E, m->eps, s, m_dev));
     rec.end(kProfLayerNorm, p + "attention_output");
-    GDC_TRY(launch_linear(w.x1, E, Lw.w1, Lw.b1, w.big, F, T, F, E, kActGelu, s, m->err));
+    GDC_TRY(launch_linear(w.x1, E, Lw.w1, Lw.b1, w.big, F, T, F, E, kActGelu, s, m->err, m_dev));
     rec.end(kProfFfnUpGemm, "");
-    GDC_TRY(launch_linear(w.big, F, Lw.w2, Lw.b2, w.tmp, E, T, E, F, kActNone, s, m->err));
+    GDC_TRY(launch_linear(w.big, F, Lw.w2, Lw.b2, w.tmp, E, T, E, F, kActNone, s, m->err, m_dev));
     rec.end(kProfFfnDownGemm, "");
-    GDC_TRY(launch_residual_layer_norm(w.tmp, w.x1, Lw.ln2_g, Lw.ln2_b, w.x, T, E, m->eps, s));
+    GDC_TRY(launch_residual_layer_norm(w.tmp, w.x1, Lw.ln2_g, Lw.ln2_b, w.x, T, E, m->eps, s, m_dev));
     rec.end(kProfLayerNorm, p + "feed_forward");
   }
-  GDC_TRY(launch_marker_gather(w.x, markers, w.mrows, int(R), Hm * O, L, E, s, m->err));
+  GDC_TRY(launch_marker_gather(w.x, markers, w.mrows, int(R), Hm * O, L, E, s, m->err, seq_off));
   GDC_TRY(launch_linear(w.mrows, E, m->cls_w0, m->cls_b0, w.mhid, m->classifier_hidden, R, m->classifier_hidden, E,
                         kActRelu, s, m->err));
   GDC_TRY(launch_classifier_out(w.mhid, m->cls_w2, m->cls_b2, marker_mask, logits, logits16, int(R),
@@ -490,6 +528,15 @@ gdc_status forward(gdc_model* m, int B, int L, int Hm, int O, const int32_t* ids
   GDC_TRY(copy_if_needed(logits, w.logits, size_t(R) * 4, s));
   if (logits16) GDC_TRY(copy_if_needed(logits16, w.logits16, size_t(R) * 2, s));
   return GDC_OK;
+}
+
+void set_row_packing(gdc_model* m, bool on) {
+  if (m->pack_rows == on) return;
+  m->pack_rows = on;
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  for (auto& g : m->graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+  m->graphs.clear();
 }
 
 gdc_status read_device_errors(gdc_model* m, cudaStream_t s) {

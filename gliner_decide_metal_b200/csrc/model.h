@@ -58,6 +58,14 @@ struct Workspace {
   // input / output staging (device)
   int32_t* ids = nullptr;
   __half* mask = nullptr;
+  // packed-row layout (kernels/pack.cu): seq_off [B + 1] (seq_off[B] = packed row count),
+  // rowmap [T] packed row -> dense position b * L + t
+  int32_t* seq_off = nullptr;
+  int32_t* rowmap = nullptr;
+  int32_t* row_order = nullptr;  // [B] attention work order (kernels/pack.cu)
+  // [64] small control block: [0, 2) attention work counter (zero between launches),
+  // [8, 13) attention work groups
+  int32_t* ctrl = nullptr;
   int32_t* marker_idx = nullptr;
   float* marker_mask = nullptr;
   float* logits = nullptr;
@@ -93,6 +101,9 @@ struct gdc_model {
   int64_t vocab = 128011;
   int classifier_hidden = 2048;
   float eps = 1e-7f;
+  // Encoder rows: packed (only positions [0, ext_b) of each batch row, see
+  // kernels/pack.cu) or the dense [B, L] grid. Both give bit-identical logits.
+  bool pack_rows = true;
 
   cudaStream_t stream = nullptr;
   std::mutex mu;
@@ -140,6 +151,9 @@ gdc_status ensure_workspace(gdc_model* m, int64_t tokens, int64_t markers);
 gdc_status forward(gdc_model* m, int batch, int seq_len, int max_heads, int max_options, const int32_t* ids,
                    const __half* mask, const int32_t* markers, const float* marker_mask, float* logits,
                    __half* logits16, cudaStream_t stream, bool named_stages);
+
+// Switches between packed and dense encoder rows; drops captured forwards when it changes.
+void set_row_packing(gdc_model* m, bool on);
 
 // Reads and clears the device error word (synchronises `stream`).
 gdc_status read_device_errors(gdc_model* m, cudaStream_t stream);

@@ -168,6 +168,18 @@ gdc_status gdc_check_errors(gdc_model* model);
 /* The model's CUDA stream (cudaStream_t) — for event timing by callers. */
 void* gdc_model_stream(gdc_model* model);
 
+/* Encoder row layout. enabled != 0 (the default; environment GDC_PACK_ROWS=0 makes dense
+ * the default): each batch row's positions [0, ext) are packed back to back and only those
+ * rows go through the encoder, ext = 1 + the last position with attention_mask > 0 or an
+ * active marker index, whichever is larger (ext = seq_len for a row with no valid
+ * position). enabled == 0: the dense [batch, seq_len] grid, as the reference computes it.
+ * The logits are bit-identical either way: positions at or past ext reach a logit neither
+ * as a gathered marker row nor as a key (their softmax weight is exactly zero). No
+ * counterpart in the reference (DeBERTa.swift:274-447 always runs the dense grid).
+ * Synchronises the model's stream and drops captured forwards when the setting changes. */
+gdc_status gdc_model_set_row_packing(gdc_model* model, int enabled);
+int gdc_model_row_packing(const gdc_model* model);
+
 /* Stage-time recording for gdc_classify_device: when enabled, CUDA events bracket
  * every kernel group; gdc_profile_read sums their device time per event name over
  * all calls since the last reset (ns) and returns the count of entries written. */

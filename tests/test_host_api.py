@@ -202,3 +202,24 @@ def test_classify_argument_checks_need_no_gpu():
     assert lib.gdc_classify(None, None, 0, ctypes.byref(out)) == 11
     assert lib.gdc_check_errors(None) == 11
     assert lib.gdc_decode(None, 1, 1, 1, None, None, None, None) == 11
+
+
+def test_packed_row_layout_rule():
+    """Extent rule of the packed encoder rows: last valid position or active marker + 1,
+    the full length for a row with no valid position; offsets are the prefix sums."""
+    import gliner_decide_metal_b200 as g
+    mask = np.zeros((4, 8), np.float16)
+    mask[0, :3] = 1
+    mask[1, [0, 5]] = 1          # hole
+    mask[3, :8] = 1
+    mk = np.zeros((4, 1, 2), np.int64)
+    mm = np.zeros((4, 1, 2), np.float32)
+    mk[0, 0] = [1, 6]
+    mm[0, 0] = [1, 1]            # active marker past the last valid token
+    mk[1, 0] = [7, 2]
+    mm[1, 0] = [0, 1]            # inactive marker past the extent does not count
+    mk[2, 0] = [4, 9]
+    mm[2, 0] = [1, 1]            # no valid position: full length
+    ext, off = g.packed_row_layout(mask, mk, mm)
+    assert list(ext) == [7, 6, 8, 8]
+    assert list(off) == [0, 7, 13, 21, 29]
