@@ -13,6 +13,11 @@
 //     barriers; both CTAs' epilogues arrive on the leader's "tmem empty" barrier.
 // Persistent over tiles (one tile sequence per pair), 2 TMEM accumulators so the
 // epilogue of one tile overlaps the main loop of the next. All waits are bounded.
+//
+// Tail split: the tiles are 256 x BN; when the last wave over the CTA pairs would be at most
+// half full, its tiles are split into two 256 x BN/2 tiles each, so that wave takes half the
+// time. The row count may come from device memory (packed encoder rows), so the split is
+// decided in the kernel; every role derives the same tile list from (M, N, pairs).
 #include <cuda.h>
 
 #include "kernels.h"
@@ -54,11 +59,37 @@ __device__ __forceinline__ float erf_as7126(float x) {
 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f)); }
 
+// One output tile: 256-row block mb, columns [n0, n0 + bn).
+struct PairTile {
+  int mb, n0, bn;
+};
+
+// Tile t of the launch's list: full-width tiles in M-fastest order, then (when the tail is
+// split) the halves of the last `rem` full-width tiles.
+struct PairTiles {
+  int num_m, n_main, rem, num_tiles, bn;
+  __device__ PairTiles(int M, int N, int BN, int pairs, bool can_split) : bn(BN) {
+    num_m = (M + 255) / 256;
+    const int num_big = num_m * (N / BN);
+    rem = pairs > 0 ? num_big % pairs : 0;
+    if (!can_split || rem == 0 || 2 * rem > pairs) rem = 0;
+    n_main = num_big - rem;
+    num_tiles = n_main + 2 * rem;
+  }
+  __device__ PairTile operator()(int t) const {
+    if (t < n_main) return PairTile{t % num_m, (t / num_m) * bn, bn};
+    const int u = t - n_main;
+    const int big = n_main + (u >> 1);
+    return PairTile{big % num_m, (big / num_m) * bn + (u & 1) * (bn / 2), bn / 2};
+  }
+};
+
 template <int BN, int ACT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                     const __grid_constant__ CUtensorMap tm_out, const __half* __restrict__ bias, int M_cap, int N,
-                     int K, int* err, const int32_t* __restrict__ m_dev) {
+                     const __grid_constant__ CUtensorMap tm_w_half, const __grid_constant__ CUtensorMap tm_out,
+                     const __half* __restrict__ bias, int M_cap, int N, int K, int* err,
+                     const int32_t* __restrict__ m_dev) {
   using S = PairShape<BN>;
   const int M = m_dev != nullptr ? min(M_cap, *m_dev) : M_cap;  // rows computed (same in both CTAs)
   extern __shared__ uint8_t smem_raw[];
@@ -77,11 +108,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = ptx::cluster_ctarank();
   const bool leader = rank == 0;
-  const int num_m = (M + 255) / 256;
-  const int num_tiles = num_m * (N / BN);
   const int kblocks = (K + kBK - 1) / kBK;  // a last half block reads TMA zero fill
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
+  // halves of BN = 256 / 128 keep the epilogue's 32-column chunks whole
+  const PairTiles tiles(M, N, BN, num_pairs, BN % 128 == 0);
+  const int num_tiles = tiles.num_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::kStages; ++s) {
@@ -109,26 +141,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       ptx::prefetch_tensor_map(&tm_a);
       ptx::prefetch_tensor_map(&tm_w);
+      ptx::prefetch_tensor_map(&tm_w_half);
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
-        const int mb = tile % num_m;
-        const int nb = tile / num_m;
+        const PairTile ti = tiles(tile);
+        const bool full_w = ti.bn == BN;
+        const int w_rows = ti.bn / 2;  // rows of W this CTA loads
+        const uint32_t tx = 2u * uint32_t(S::kABytes + 2 * w_rows * kAtomK * 2);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1u, err)) {
             ok = false;
             break;
           }
           const uint32_t leader_full = ptx::mapa_shared(ptx::smem_u32(&full[stage]), 0);
-          if (leader) ptx::mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
+          if (leader) ptx::mbar_arrive_expect_tx(&full[stage], tx);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             ptx::tma_load_2d_pair(s_a + stage * S::kABytes + h * S::kAHalf, &tm_a, kb * kBK + h * kAtomK,
-                                  mb * 256 + int(rank) * 128, leader_full);
-            ptx::tma_load_2d_pair(s_b + stage * S::kBBytes + h * S::kBHalf, &tm_w, kb * kBK + h * kAtomK,
-                                  nb * BN + int(rank) * (BN / 2), leader_full);
+                                  ti.mb * 256 + int(rank) * 128, leader_full);
+            ptx::tma_load_2d_pair(s_b + stage * S::kBBytes + h * S::kBHalf, full_w ? &tm_w : &tm_w_half,
+                                  kb * kBK + h * kAtomK, ti.n0 + int(rank) * w_rows, leader_full);
           }
           ++issued;
           if (++stage == S::kStages) {
@@ -154,7 +189,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = ptx::idesc_f16_f32(256, BN);
+      constexpr uint32_t idesc_full = ptx::idesc_f16_f32(256, BN);
+      constexpr uint32_t idesc_half = ptx::idesc_f16_f32(256, BN / 2);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -168,6 +204,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        const uint32_t idesc = tiles(tile).bn == BN ? idesc_full : idesc_half;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!ptx::mbar_wait(&full[stage], phase, err)) {
             ok = false;
@@ -204,7 +241,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // of 16-byte stores to 32 different rows.
     const int quarter = warp & 3;
     const int col_half = (warp - 2) >> 2;
-    constexpr int kHalfCols = BN / 2;
     uint8_t* box = s_out + (warp - 2) * 2048;
     uint8_t* box_row = box + lane * 64;
     const uint32_t box_swz = uint32_t((lane >> 1) & 3);
@@ -214,17 +250,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t aphase = (local >> 1) & 1;
       if (!ptx::mbar_wait(&tfull[acc], aphase, err)) break;
       ptx::tc_fence_after();
-      const int mb = tile % num_m;
-      const int nb = tile / num_m;
-      const int row0 = mb * 256 + int(rank) * 128 + quarter * 32;
+      const PairTile ti = tiles(tile);
+      const int half_cols = ti.bn / 2;  // columns of this warp's half of the tile
+      const int row0 = ti.mb * 256 + int(rank) * 128 + quarter * 32;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < kHalfCols; c += 32) {
-        const int col = col_half * kHalfCols + c;
+      for (int c = 0; c < half_cols; c += 32) {
+        const int col = col_half * half_cols + c;
         uint32_t r[32];
         ptx::tmem_ld_32x32b_x32(t_row + uint32_t(col), r);
         ptx::tmem_wait_ld();
-        const int n0 = nb * BN + col;
+        const int n0 = ti.n0 + col;
         const uint4* bsrc = reinterpret_cast<const uint4*>(bias + n0);
         uint32_t packed[16];
 #pragma unroll
@@ -277,8 +313,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, int ACT>
-gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const __half* bias,
-                               int M, int N, int K, cudaStream_t stream, int* err, const int32_t* m_dev) {
+gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& twh,
+                               const CUtensorMap& to, const __half* bias, int M, int N, int K, cudaStream_t stream,
+                               int* err, const int32_t* m_dev) {
   using S = PairShape<BN>;
   auto kern = gemm_pair_kernel<BN, ACT>;
   static bool configured[64] = {};
@@ -292,7 +329,7 @@ gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, con
   const int num_tiles = ((M + 255) / 256) * (N / BN);
   const int pairs_avail = device_sm_count(dev) / 2;
   const int pairs = num_tiles < pairs_avail ? num_tiles : pairs_avail;
-  kern<<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(ta, tw, to, bias, M, N, K, err, m_dev);
+  kern<<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(ta, tw, twh, to, bias, M, N, K, err, m_dev);
   return check_launch("gemm_pair_kernel");
 }
 
@@ -321,18 +358,21 @@ gdc_status launch_linear_pair(const __half* a, int64_t lda, const __half* w, con
                               const int32_t* m_dev) {
   int dev = 0;
   cudaGetDevice(&dev);
-  const int bn = choose_bn(M, N, device_sm_count(dev) / 2);
+  // With a device row count the kernel splits a sparse last wave itself; full-width 256
+  // tiles are then the best start wherever N allows them.
+  const int bn = (m_dev != nullptr && N % 256 == 0) ? 256 : choose_bn(M, N, device_sm_count(dev) / 2);
   if (bn == 0) return set_error(GDC_ERR_UNSUPPORTED, "linear: N=%d is not a multiple of 128", N);
-  CUtensorMap ta, tw, to;
+  CUtensorMap ta, tw, twh, to;
   GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), 128));
   GDC_TRY(make_tmap_2d(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 2)));
+  GDC_TRY(make_tmap_2d(&twh, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 4)));
   GDC_TRY(make_tmap_2d_out32(&to, out, uint64_t(M), uint64_t(N), uint64_t(ldo)));
   const int m = int(M);
 #define GDC_PAIR_CASE(BNV)                                                                              \
   if (bn == BNV) {                                                                                      \
-    if (act == kActGelu) return launch_pair_variant<BNV, kActGelu>(ta, tw, to, bias, m, N, K, stream, err, m_dev); \
-    if (act == kActRelu) return launch_pair_variant<BNV, kActRelu>(ta, tw, to, bias, m, N, K, stream, err, m_dev); \
-    return launch_pair_variant<BNV, kActNone>(ta, tw, to, bias, m, N, K, stream, err, m_dev); \
+    if (act == kActGelu) return launch_pair_variant<BNV, kActGelu>(ta, tw, twh, to, bias, m, N, K, stream, err, m_dev); \
+    if (act == kActRelu) return launch_pair_variant<BNV, kActRelu>(ta, tw, twh, to, bias, m, N, K, stream, err, m_dev); \
+    return launch_pair_variant<BNV, kActNone>(ta, tw, twh, to, bias, m, N, K, stream, err, m_dev); \
   }
   GDC_PAIR_CASE(256)
   GDC_PAIR_CASE(192)
