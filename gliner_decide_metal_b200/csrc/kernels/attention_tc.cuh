@@ -22,8 +22,8 @@
 //   rows  drain P -> fp16 in SMEM (row k) over the consumed windows; gather c2p from the
 //         own row and p2c across rows, add the fp16 relative bias to S, online softmax
 //         (fp32), write fp16 probabilities as a K-major SW128 operand
-//   MMA   O_j = Prob . V (cols 384-447, V as an MN-major operand)
-//   rows  O = O * exp(m_old - m_new) + O_j in registers
+//   MMA   O += Prob . V (cols 384-447, V as an MN-major operand); before it the rows
+//         rescale O in TMEM by exp(m_old - m_new) when a row's running max changed
 // Threads: 4 * kParts row warps; warp w owns TMEM lane quarter w % 4 (query rows / key rows
 // 32*(w%4)..+32) and part w / 4 of the columns / keys of every phase. The next warp's lane 0
 // issues the MMAs; the last warp issues the TMA loads (and scans key masks). Every wait is a
@@ -66,13 +66,13 @@ constexpr int kOffRed = kOffAdd + 512;         // cross-part max exchange, 4 x 1
 constexpr int kOffRedL = kOffRed + 2048;       // cross-part denominator exchange, 4 x 128 f32
 constexpr int kOffFlags = kOffRedL + 2048;     // per item (2 slots): key-tile mask, then item index
 constexpr int kOffBar = kOffFlags + 64;        // mbarriers
-constexpr int kNumBars = 14;
+constexpr int kNumBars = 15;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
 
 enum Bar {
   kBarQ = 0, kBarKV0, kBarKV1, kBarSC, kBarCDone, kBarP, kBarProbs, kBarO, kBarODone, kBarRow, kBarDrain, kBarFlags,
-  kBarKVFree0, kBarKVFree1
+  kBarKVFree0, kBarKVFree1, kBarScored
 };
 
 constexpr float kInvSqrt192f = 0.07216878364870322f;
@@ -325,8 +325,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool first = true;
       for (kt = next_tile(tmask, -1); kt >= 0; kt = next_tile(tmask, kt)) {
         if (lane == 0 && np > 0) {
-          // the previous pair's gathers are done: windows (and Q) are free
-          ok = ptx::mbar_wait_sleep(&bars[kBarProbs], uint32_t((np - 1) & 1), err);
+          // the previous pair's gathers are done (its P rows in the window region and its C
+          // rows are no longer read): windows and Q are free while its exp phase runs
+          ok = ptx::mbar_wait_sleep(&bars[kBarScored], uint32_t((np - 1) & 1), err);
           // PV of pair np-2, the last reader of this K / V buffer, has completed
           if (ok && np > 1)
             ok = ptx::mbar_wait_sleep(&bars[kBarKVFree0 + (np & 1)], uint32_t(((np - 2) >> 1) & 1), err);
@@ -375,8 +376,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && lane == 0) {
       // End of the work list: item -1. Published only after the last pair's gathers, so
       // every consumer has already seen the previous publication (a barrier phase cannot
-      // complete twice ahead of a waiter).
-      if (np == 0 || ptx::mbar_wait_sleep(&bars[kBarProbs], uint32_t((np - 1) & 1), err)) {
+      // complete twice ahead of a waiter). The wait is on kBarScored, which this warp has
+      // followed pair by pair: a parity wait is only exact on a barrier at most one phase
+      // ahead of it, and kBarProbs, never waited here before, may still be two behind.
+      if (np == 0 || ptx::mbar_wait_sleep(&bars[kBarScored], uint32_t((np - 1) & 1), err)) {
         s_flags[item_idx & 1] = 0;
         s_item[item_idx & 1] = -1;
         ptx::mbar_arrive(&bars[kBarFlags]);
@@ -552,6 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        if (threadIdx.x == 0) ptx::mbar_arrive(&bars[kBarScored]);  // the producer may load the next windows
         float m_tile = s_red[t];
 #pragma unroll
         for (int pp = 1; pp < kParts; ++pp) m_tile = fmaxf(m_tile, s_red[pp * 128 + t]);
