@@ -383,7 +383,9 @@ def main():
     tpath = ROOT / "profiles" / "gemm_traffic.json"
     if tpath.exists():
         try:
-            traffic = json.loads(tpath.read_text()).get("bytes_per_launch")
+            tj = json.loads(tpath.read_text())
+            # the capture is one batch's launches; scale to this run's mean packed rows
+            traffic = tj["bytes_per_launch"] * (rows_timed / args.steps) / tj.get("packed_rows", BATCH * SEQ)
         except Exception:
             traffic = None
     roofline = {"kernel": "gemm_pair_kernel (cta_group::2 tcgen05; QKV / out / FFN-up / FFN-down projections)",
@@ -395,7 +397,8 @@ def main():
                 "peak_source": f"{peaks['source']} bf16_tflops_sustained (kernel timed inside a long step)",
                 "traffic": traffic,
                 "traffic_source": "profiles/gemm_traffic.json: ncu dram__bytes_read.sum + dram__bytes_write.sum per "
-                                  "launch, layer-0 projections of this workload averaged",
+                                  "launch, layer-0 projections of one batch of this workload averaged, scaled by "
+                                  "this run's mean packed rows over the captured batch's",
                 "algorithmic_bytes_per_launch_avg": GEMM_BYTES_PER_TOKEN * rows_timed / args.steps / 4
                 + GEMM_WEIGHT_BYTES / 4,
                 "algorithmic_units": f"{rows_timed / args.steps:.1f} packed rows per step (of {BATCH * SEQ} dense)",
