@@ -230,8 +230,13 @@ gdc_status gdc_classify(gdc_model* m, const gdc_input* in, int collect_profile, 
   if (collect_profile) m->stage_names.clear();
   const bool prev_prof = m->profiling;
   if (collect_profile) m->profiling = false;  // named stages only
+  // Packed rows only pay off when some row ends in padding; the staged fp16 mask says so.
+  bool dense_hint = true;
+  const uint16_t* mask16 = reinterpret_cast<const uint16_t*>(w.h_in + T * 4);
+  for (int32_t b = 0; b < in->batch && dense_hint; ++b)
+    dense_hint = f16_bits_to_f32(mask16[int64_t(b) * in->seq_len + in->seq_len - 1]) > 0.f;
   gdc_status st = forward(m, in->batch, in->seq_len, in->max_heads, in->max_options, w.ids, w.mask, w.marker_idx,
-                          w.marker_mask, w.logits, w.logits16, s, collect_profile != 0);
+                          w.marker_mask, w.logits, w.logits16, s, collect_profile != 0, dense_hint);
   m->profiling = prev_prof;
   if (st != GDC_OK) return st;
   GDC_CUDA_TRY(cudaMemcpyAsync(w.h_out, w.logits, size_t(R) * 4, cudaMemcpyDeviceToHost, s));

@@ -53,9 +53,15 @@ gdc_status launch_attention(const __half* qkv, const __half* pos_qk, const __hal
   if (items > (1ll << 30)) return set_error(GDC_ERR_UNSUPPORTED, "attention: too many work items");
   const int sms = device_sm_count(dev);
   const int grid = items < sms ? int(items) : sms;  // persistent: one CTA per SM
+  AttentionWork w = work;
+  if (items <= grid) {
+    // one item per CTA at most: the static split is already balanced and needs no atomics
+    w.counter = nullptr;
+    w.row_order = nullptr;
+    w.groups = nullptr;
+  }
   attn::attention_tc_kernel<<<grid, attn::kThreads, attn::kSmemBytes, stream>>>(tm_qkv, tm_pos, key_mask, rel_table,
-                                                                                ctx, batch, seq_len, heads, err,
-                                                                                work);
+                                                                                ctx, batch, seq_len, heads, err, w);
   return check_launch("attention_tc_kernel");
 }
 

@@ -61,10 +61,11 @@ constexpr int kOffV = kOffK + 32768;           // V tiles (2 buffers)   32 KB
 constexpr int kOffW = kOffV + 32768;           // PK | PQ windows 2 x 32 KB, then P rows (64 KB)
 constexpr int kOffC = kOffW + 65536;           // C rows 64 KB, then probabilities (32 KB)
 constexpr int kOffTab = kOffC + 65536;         // relative index table, 1024 x int16
-constexpr int kOffAdd = kOffTab + 2048;        // per key of the tile: 0 valid, -65504 masked, -inf beyond L
-constexpr int kOffRed = kOffAdd + 512;         // cross-part max exchange, 4 x 128 f32
+constexpr int kOffAdd = kOffTab + 2048;        // per item (2 slots) and key: 0 valid, -65504 masked, -inf past
+                                               // the extent; 2 x 512 f32
+constexpr int kOffRed = kOffAdd + 4096;        // cross-part max exchange, 4 x 128 f32
 constexpr int kOffRedL = kOffRed + 2048;       // cross-part denominator exchange, 4 x 128 f32
-constexpr int kOffFlags = kOffRedL + 2048;     // per item (2 slots): key-tile mask, then item index
+constexpr int kOffFlags = kOffRedL + 2048;     // per item (2 slots): key-tile mask, item index, extent, row base
 constexpr int kOffBar = kOffFlags + 64;        // mbarriers
 constexpr int kNumBars = 15;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
@@ -212,6 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* s_red_l = reinterpret_cast<float*>(sm + kOffRedL);
   volatile uint32_t* s_flags = reinterpret_cast<volatile uint32_t*>(sm + kOffFlags);
   volatile int32_t* s_item = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 16);
+  volatile int32_t* s_ext = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 32);
+  volatile int32_t* s_row = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 48);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffTmemSlot);
 
@@ -311,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t tmask = 0;
     Item it{};
     MaskChunk pre{};  // key-mask registers prefetched for the upcoming item (batch row pre_b)
-    int pre_b = -1;
+    int pre_b = -1, pre_ext = 0, pre_row = 0;  // and that row's extent / first qkv row
     bool ok = true;
     while (item >= 0) {
       // pair np is the first of item `item`: publish its tile mask and load Q
@@ -319,7 +322,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (pre_b != it.b) {
         pre = load_mask_chunk(key_mask, (long long)it.b * L, L);
         pre_b = it.b;
+        pre_ext = extent(it.b);
+        pre_row = row_base(it.b);
       }
+      const int it_ext = pre_ext, it_row = pre_row;
       tmask = key_tile_mask(pre, n_kt);
       int nxt = -1;
       bool first = true;
@@ -334,18 +340,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ok = __shfl_sync(0xffffffffu, ok, 0) != 0;
         if (!ok) break;
+        if (first) {
+          // the item's additive key mask, one value per key (lane l: keys 8l.. and 256 + 8l..)
+          float* sa = s_add + (item_idx & 1) * 512;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const __half* mh = reinterpret_cast<const __half*>(&pre.v[hh]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int k = hh * 256 + lane * 8 + j;
+              sa[k] = k >= it_ext ? -INFINITY : (__half2float(mh[j]) > 0.f ? 0.f : -65504.0f);
+            }
+          }
+          __syncwarp();
+        }
         if (lane == 0) {
           if (first) {
             s_flags[item_idx & 1] = tmask;
             s_item[item_idx & 1] = item;
+            s_ext[item_idx & 1] = it_ext;
+            s_row[item_idx & 1] = it_row;
             ptx::mbar_arrive(&bars[kBarFlags]);  // release: mask and item are visible to the consumers
             ptx::mbar_arrive_expect_tx(&bars[kBarQ], 16384);
-            ptx::tma_load_2d(sQ, &tm_qkv, it.h * 64, row_base(it.b) + it.qt * kTile, &bars[kBarQ]);
+            ptx::tma_load_2d(sQ, &tm_qkv, it.h * 64, it_row + it.qt * kTile, &bars[kBarQ]);
           }
           const int buf = np & 1;
           const int k0 = kt * kTile;
           const int lo = window_lo(it.qt * kTile, k0);
-          const int krow = row_base(it.b) + k0;
+          const int krow = it_row + k0;
           uint64_t* bar = &bars[kBarKV0 + buf];
           ptx::mbar_arrive_expect_tx(bar, 2 * 16384 + 2 * 32768);
           ptx::tma_load_2d(sm + kOffK + buf * 16384, &tm_qkv, E + it.h * 64, krow, bar);
@@ -362,6 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (nb != pre_b) {
               pre = load_mask_chunk(key_mask, (long long)nb * L, L);  // consumed at the next item
               pre_b = nb;
+              pre_ext = extent(nb);
+              pre_row = row_base(nb);
             }
           }
         }
@@ -488,19 +512,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Item it = decode_item(item, n_kt, heads);
       const int q0 = it.qt * kTile;
       const int q = q0 + t;
-      const long long row0 = (long long)it.b * L;  // key mask row ([B, L] in both layouts)
-      const long long orow0 = row_base(it.b);     // qkv / ctx row of position 0
-      const int ext = extent(it.b);
+      const long long orow0 = s_row[item_idx & 1];  // qkv / ctx row of position 0
+      const int ext = s_ext[item_idx & 1];
+      const float* s_add_item = s_add + (item_idx & 1) * 512;
       float m_run = -INFINITY, l_part = 0.f;
       bool first_pair = true;
       for (int kt = next_tile(tmask, -1); kt >= 0; kt = next_tile(tmask, kt), ++np) {
         const int k0 = kt * kTile;
         const int lo = window_lo(q0, k0);
         const uint32_t par = uint32_t(np & 1);
-        if (part == 0) {
-          const int k = k0 + t;
-          s_add[t] = k >= ext ? -INFINITY : (__half2float(key_mask[row0 + k]) > 0.f ? 0.f : -65504.0f);
-        }
+        const float* s_add_pair = s_add_item + k0;
         // ---- drain C (own query row, this part's 64 columns)
         if (!ptx::mbar_wait_sleep(&bars[kBarSC], par, err)) {
           ok = false;
@@ -540,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const __half pv =
                 *reinterpret_cast<const __half*>(sPst + uint32_t(kk) * 512u + (w2 ^ (uint32_t(kk & 7) << 4)));
             const float rb = __half2float(__float2half_rn(__half2float(__hadd(cv, pv)) * kInvScale16));
-            const float add = s_add[kk];
+            const float add = s_add_pair[kk];
             const float sv = fmaf(__uint_as_float(sraw[u]), kInvSqrt192f, add == 0.f ? rb : add);
             sraw[u] = __float_as_uint(sv);
             part_max = fmaxf(part_max, sv);

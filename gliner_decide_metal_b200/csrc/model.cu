@@ -374,7 +374,7 @@ namespace {
 // The kernel sequence of the forward (DeBERTa.swift:274-447) on stream s.
 gdc_status enqueue_forward(gdc_model* m, int B, int L, int Hm, int O, const int32_t* ids, const __half* mask,
                            const int32_t* markers, const float* marker_mask, float* logits, __half* logits16,
-                           cudaStream_t s, StageRecorder& rec) {
+                           cudaStream_t s, StageRecorder& rec, bool pack) {
   const int64_t T = int64_t(B) * L;
   const int64_t R = int64_t(B) * Hm * O;
   const int E = m->hidden, F = m->inter;
@@ -389,7 +389,7 @@ gdc_status enqueue_forward(gdc_model* m, int B, int L, int Hm, int O, const int3
   AttentionWork work;
   work.counter = w.ctrl;
   rec.begin();
-  if (m->pack_rows) {
+  if (pack) {
     GDC_TRY(launch_row_pack(mask, markers, marker_mask, B, L, Hm * O, w.seq_off, w.rowmap, w.row_order, w.ctrl + 8,
                             s));
     seq_off = w.seq_off;
@@ -439,19 +439,19 @@ bool graphs_enabled() {
 
 // The graph slot of a shape (created on first use; the least recently used slot is
 // recycled beyond 8 shapes).
-ForwardGraph& graph_slot(gdc_model* m, int B, int L, int Hm, int O) {
+ForwardGraph& graph_slot(gdc_model* m, int B, int L, int Hm, int O, bool packed) {
   for (auto& g : m->graphs)
-    if (g.batch == B && g.seq_len == L && g.max_heads == Hm && g.max_options == O) return g;
+    if (g.batch == B && g.seq_len == L && g.max_heads == Hm && g.max_options == O && g.packed == packed) return g;
   if (m->graphs.size() >= 8) {
     auto it = std::min_element(m->graphs.begin(), m->graphs.end(),
                                [](const ForwardGraph& x, const ForwardGraph& y) { return x.last_use < y.last_use; });
     if (it->exec) cudaGraphExecDestroy(it->exec);
     *it = ForwardGraph{};
-    it->batch = B, it->seq_len = L, it->max_heads = Hm, it->max_options = O;
+    it->batch = B, it->seq_len = L, it->max_heads = Hm, it->max_options = O, it->packed = packed;
     return *it;
   }
   ForwardGraph g;
-  g.batch = B, g.seq_len = L, g.max_heads = Hm, g.max_options = O;
+  g.batch = B, g.seq_len = L, g.max_heads = Hm, g.max_options = O, g.packed = packed;
   m->graphs.push_back(g);
   return m->graphs.back();
 }
@@ -466,7 +466,7 @@ gdc_status capture_graph(gdc_model* m, ForwardGraph& g, cudaStream_t s) {
   StageRecorder off{m, s, false, false};
   GDC_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   const gdc_status st = enqueue_forward(m, g.batch, g.seq_len, g.max_heads, g.max_options, w.ids, w.mask,
-                                        w.marker_idx, w.marker_mask, w.logits, w.logits16, s, off);
+                                        w.marker_idx, w.marker_mask, w.logits, w.logits16, s, off, g.packed);
   cudaGraph_t graph = nullptr;
   const cudaError_t ce = cudaStreamEndCapture(s, &graph);
   if (st != GDC_OK) {
@@ -494,8 +494,9 @@ gdc_status copy_if_needed(void* dst, const void* src, size_t bytes, cudaStream_t
 
 gdc_status forward(gdc_model* m, int B, int L, int Hm, int O, const int32_t* ids, const __half* mask,
                    const int32_t* markers, const float* marker_mask, float* logits, __half* logits16,
-                   cudaStream_t s, bool named_stages) {
+                   cudaStream_t s, bool named_stages, bool dense_hint) {
   const int64_t T = int64_t(B) * L;
+  const bool pack = m->pack_rows && !dense_hint;
   const int64_t R = int64_t(B) * Hm * O;
   GDC_TRY(ensure_workspace(m, T, R));
   Workspace& w = m->ws;
@@ -509,16 +510,18 @@ gdc_status forward(gdc_model* m, int B, int L, int Hm, int O, const int32_t* ids
       m->events.push_back(e);
       m->event_class.push_back(-1);
     }
-    return enqueue_forward(m, B, L, Hm, O, ids, mask, markers, marker_mask, logits, logits16, s, rec);
+    return enqueue_forward(m, B, L, Hm, O, ids, mask, markers, marker_mask, logits, logits16, s, rec, pack);
   }
-  if (!graphs_enabled()) return enqueue_forward(m, B, L, Hm, O, ids, mask, markers, marker_mask, logits, logits16, s, rec);
+  if (!graphs_enabled())
+    return enqueue_forward(m, B, L, Hm, O, ids, mask, markers, marker_mask, logits, logits16, s, rec, pack);
   // Replay path: the graph reads the workspace staging buffers and writes ws.logits /
   // ws.logits16, so caller buffers elsewhere are copied in and out around it. The first
   // call of a shape runs eagerly (one-time kernel attribute set-up happens outside any
   // capture); the second captures the graph.
-  ForwardGraph& g = graph_slot(m, B, L, Hm, O);
+  ForwardGraph& g = graph_slot(m, B, L, Hm, O, pack);
   g.last_use = ++m->graph_clock;
-  if (g.calls++ == 0) return enqueue_forward(m, B, L, Hm, O, ids, mask, markers, marker_mask, logits, logits16, s, rec);
+  if (g.calls++ == 0)
+    return enqueue_forward(m, B, L, Hm, O, ids, mask, markers, marker_mask, logits, logits16, s, rec, pack);
   if (g.exec == nullptr || g.generation != w.generation) GDC_TRY(capture_graph(m, g, s));
   GDC_TRY(copy_if_needed(w.ids, ids, size_t(T) * 4, s));
   GDC_TRY(copy_if_needed(w.mask, mask, size_t(T) * 2, s));

@@ -83,6 +83,7 @@ struct Workspace {
 // ws.logits / ws.logits16; valid while the workspace generation is unchanged.
 struct ForwardGraph {
   int batch = 0, seq_len = 0, max_heads = 0, max_options = 0;
+  bool packed = false;  // row layout the graph was captured with
   int generation = -1;
   int calls = 0;                  // eager calls seen for this shape (captured on the second)
   cudaGraphExec_t exec = nullptr;
@@ -148,9 +149,11 @@ gdc_status ensure_workspace(gdc_model* m, int64_t tokens, int64_t markers);
 
 // Runs the forward on device-resident inputs (ws or caller buffers) on `stream`.
 // named_stages: record the reference's stage events into m->stage_names / events.
+// dense_hint: the caller knows this batch has no padding past any row's last valid position,
+// so packed rows would save nothing; the call then runs on the dense grid.
 gdc_status forward(gdc_model* m, int batch, int seq_len, int max_heads, int max_options, const int32_t* ids,
                    const __half* mask, const int32_t* markers, const float* marker_mask, float* logits,
-                   __half* logits16, cudaStream_t stream, bool named_stages);
+                   __half* logits16, cudaStream_t stream, bool named_stages, bool dense_hint = false);
 
 // Switches between packed and dense encoder rows; drops captured forwards when it changes.
 void set_row_packing(gdc_model* m, bool on);

@@ -176,6 +176,8 @@ void* gdc_model_stream(gdc_model* model);
  * The logits are bit-identical either way: positions at or past ext reach a logit neither
  * as a gathered marker row nor as a key (their softmax weight is exactly zero). No
  * counterpart in the reference (DeBERTa.swift:274-447 always runs the dense grid).
+ * gdc_classify runs a batch whose every row ends in a valid position on the dense grid
+ * (there is nothing to remove; the packing pass would only add work).
  * Synchronises the model's stream and drops captured forwards when the setting changes. */
 gdc_status gdc_model_set_row_packing(gdc_model* model, int enabled);
 int gdc_model_row_packing(const gdc_model* model);
