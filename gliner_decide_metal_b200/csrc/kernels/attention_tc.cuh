@@ -86,6 +86,14 @@ __device__ __forceinline__ uint32_t rowblk_off(int row, int col) {
   return uint32_t(row) * 512u + ((uint32_t(col) << 1) ^ (uint32_t(row & 7) << 4));
 }
 
+// 2^x with the hardware approximation (MUFU.EX2); the exp phase computes
+// exp(s - m) = 2^(s log2 e - m log2 e) with one FFMA per probability.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Bounded rendezvous of all row threads.
 struct RowSync {
   uint64_t* bar;
@@ -582,7 +590,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int pp = 1; pp < kParts; ++pp) m_tile = fmaxf(m_tile, s_red[pp * 128 + t]);
         const float m_new = fmaxf(m_run, m_tile);
         const float alpha = __expf(m_run - m_new);
+        // the softmax denominator sums the fp32 exponentials (the reference's SDPA softmax is
+        // fp32); the PV MMA multiplies their fp16 roundings
         float psum = 0.f;
+        const float m_l2 = m_new * 1.4426950408889634f;
 #pragma unroll
         for (int c = 0; c < kKeysPP / 32; ++c) {
           uint32_t sv[32];
@@ -594,10 +605,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int i = j * 8 + 2 * e;
-              const __half2 p2 = __floats2half2_rn(__expf(__uint_as_float(sv[i]) - m_new),
-                                                   __expf(__uint_as_float(sv[i + 1]) - m_new));
-              const float2 pf = __half22float2(p2);
-              psum += pf.x + pf.y;
+              const float e0 = ex2_approx(fmaf(__uint_as_float(sv[i]), 1.4426950408889634f, -m_l2));
+              const float e1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), 1.4426950408889634f, -m_l2));
+              const __half2 p2 = __floats2half2_rn(e0, e1);
+              psum += e0 + e1;
               pk[e] = *reinterpret_cast<const uint32_t*>(&p2);
             }
             // K-major SW128 operand: atom kb / 64 holds keys 64*(kb/64)..+63 of row t
