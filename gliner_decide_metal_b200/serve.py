@@ -7,17 +7,25 @@ The reference reads JSONL lines ``{id, text, tasks}``, tokenises each with
 decodes every row's tasks (RawCLI.swift:182-223) and writes a JSON array of results in
 input order, each with the inference time of its batch divided by the batch size.
 
-Tokenisation needs the model's ``tokenizer.json``, which this backend does not ship, so the
-loop here starts one step later: each example carries the token ids the tokenizer would
-produce (schema + text, before padding) and the positions of its ``[L]`` label markers per
-task. Bucket choice, padding and marker layout are the reference's (``gdc_layout_row``);
-grouping, chunking, decoding and the output format are RawCLI's. ``--devices`` splits each
-chunk's rows across GPUs (``gdc_classify_sharded``).
+With ``--tokenizer DIR`` (a directory holding the checkpoint's ``tokenizer.json`` and
+``tokenizer_config.json``) the lines are the reference's own ``RawExample`` JSON
+(RawCLI.swift:11-15)::
 
-JSONL input line::
+    {"id": "...", "text": "...",
+     "tasks": [{"name": "...", "labels": [...], "multiLabel": false,
+                "prompt": "...", "labelDescriptions": {"label": "..."}}]}
+
+and each one goes through ``NativeDecisionTokenizer.make_input`` (``tokenizer.py``), timed
+as its preprocessing. Without a tokenizer the loop starts one step later: each line carries
+the token ids the tokenizer would produce (schema + text, before padding) and the positions
+of its ``[L]`` label markers per task::
 
     {"id": "...", "token_ids": [...],
      "tasks": [{"name": "...", "labels": [...], "multi_label": false, "marker_positions": [...]}]}
+
+Bucket choice, padding and marker layout are the reference's (``gdc_layout_row``);
+grouping, chunking, decoding and the output format are RawCLI's. ``--devices`` splits each
+chunk's rows across GPUs (``gdc_classify_sharded``).
 
 Output (``--output`` or stdout): the reference's JSON array
 ``[{"id", "predictions": [{"task", "labels", "probabilities"}], "preprocessingMilliseconds",
@@ -79,9 +87,33 @@ def load_jsonl(path) -> List[TokenizedExample]:
 
 
 @dataclass
+class RawExample:
+    """``RawExample`` (RawCLI.swift:11-15): an id, the text and its decision tasks."""
+    id: str
+    text: str
+    tasks: List[DecisionTask]
+
+
+def parse_raw_example(obj: dict) -> RawExample:
+    """The reference's JSON keys (``DecisionTask`` Codable: name, labels, multiLabel, prompt,
+    labelDescriptions; ``multi_label`` is accepted too)."""
+    tasks = []
+    for t in obj["tasks"]:
+        multi = t.get("multiLabel", t.get("multi_label", False))
+        tasks.append(DecisionTask(str(t["name"]), tuple(str(x) for x in t["labels"]), bool(multi),
+                                  t.get("prompt"), t.get("labelDescriptions", t.get("label_descriptions"))))
+    return RawExample(str(obj["id"]), str(obj.get("text", "")), tasks)
+
+
+def load_raw_jsonl(path) -> List[RawExample]:
+    with open(path, "r", encoding="utf-8") as f:
+        return [parse_raw_example(json.loads(line)) for line in f if line.strip()]
+
+
+@dataclass
 class _Pending:
     index: int
-    example: TokenizedExample
+    example: object  # TokenizedExample or RawExample (id, tasks)
     input: DecisionInput
     preprocessing_ms: float
 
@@ -110,6 +142,24 @@ def run_examples(models, examples: Sequence[TokenizedExample], buckets=DEFAULT_B
         t0 = time.perf_counter()
         inp = make_input_from_tokens(ex.token_ids, ex.marker_positions, buckets)
         pending.append(_Pending(i, ex, inp, (time.perf_counter() - t0) * 1e3))
+    return _classify_pending(models, pending, batch_size)
+
+
+def run_raw_examples(models, tokenizer, examples: Sequence[RawExample], buckets=DEFAULT_BUCKETS,
+                     batch_size: int = 32) -> List[RawResult]:
+    """RawCLI.runJSONL (RawCLI.swift:104-171) from the raw text: ``makeInput`` per row (its
+    time is the row's preprocessing), then grouping, chunking and decoding as above."""
+    if batch_size <= 0:
+        raise ValueError("batch_size must be positive")
+    pending: List[_Pending] = []
+    for i, ex in enumerate(examples):
+        t0 = time.perf_counter()
+        inp = tokenizer.make_input(ex.text, ex.tasks, buckets)
+        pending.append(_Pending(i, ex, inp, (time.perf_counter() - t0) * 1e3))
+    return _classify_pending(models, pending, batch_size)
+
+
+def _classify_pending(models, pending: Sequence["_Pending"], batch_size: int) -> List[RawResult]:
     groups: Dict[Tuple[int, int, int], List[_Pending]] = {}
     for p in pending:
         _, L, hm, o = p.input.shape
@@ -143,6 +193,8 @@ def main(argv=None) -> int:
     src.add_argument("--jsonl", help="pre-tokenised examples, one JSON object per line")
     src.add_argument("--synthetic-rows", type=int, help="seeded BASELINE config 3 rows instead of --jsonl")
     ap.add_argument("--weights", required=True, help="fp16 safetensors weights")
+    ap.add_argument("--tokenizer", default=None, help="directory with tokenizer.json / tokenizer_config.json: "
+                                                       "--jsonl lines are RawExample {id, text, tasks}")
     ap.add_argument("--buckets", default=",".join(str(b) for b in DEFAULT_BUCKETS))
     ap.add_argument("--batch-size", type=int, default=32)
     ap.add_argument("--devices", default="0", help="comma-separated CUDA devices; rows of a chunk are split")
@@ -154,11 +206,24 @@ def main(argv=None) -> int:
     cfg = DeBERTaV2Configuration(num_hidden_layers=args.layers, vocab_size=args.vocab)
     models = [GLiNERDecideClassifier(args.weights, configuration=cfg, device=int(d)) for d in args.devices.split(",")]
     try:
-        examples = load_jsonl(args.jsonl) if args.jsonl else synthetic_examples(args.synthetic_rows, buckets)
+        if args.tokenizer:
+            from .tokenizer import NativeDecisionTokenizer
+            if not args.jsonl:
+                ap.error("--tokenizer reads --jsonl RawExample lines")
+            tok = NativeDecisionTokenizer(args.tokenizer)
+            examples = load_raw_jsonl(args.jsonl)
+
+            def run(rows):
+                return run_raw_examples(models, tok, rows, buckets, args.batch_size)
+        else:
+            examples = load_jsonl(args.jsonl) if args.jsonl else synthetic_examples(args.synthetic_rows, buckets)
+
+            def run(rows):
+                return run_examples(models, rows, buckets, args.batch_size)
         print(f"loaded {len(examples)} examples", file=sys.stderr)
-        run_examples(models, examples[:min(len(examples), args.batch_size)], buckets, args.batch_size)  # warm-up
+        run(examples[:min(len(examples), args.batch_size)])  # warm-up
         t0 = time.perf_counter()
-        results = run_examples(models, examples, buckets, args.batch_size)
+        results = run(examples)
         dt = time.perf_counter() - t0
         print(f"rows: {len(examples)} total_ms: {dt * 1e3:.1f} rows_per_sec: {len(examples) / dt:.1f}",
               file=sys.stderr)

@@ -97,3 +97,39 @@ def test_benchcli_batch_and_latency_modes(weights_file, tmp_path, capsys):
     assert benchcli.main(common + ["--iterations", "5", "--warmup", "1", "--profile"]) == 0
     out = capsys.readouterr().out
     assert "p50_ms" in out and "p95_ms" in out and "layer_1_feed_forward" in out
+
+
+def test_raw_text_serving_matches_oracle(weights_file, tmp_path):
+    """RawExample lines through the native tokenizer (synthetic Unigram tokenizer.json built
+    with the tokenizers library) and the serving loop, against the oracle on the same rows."""
+    import json
+    import gliner_decide_metal_b200 as g
+    from gliner_decide_metal_b200 import serve
+    from gliner_decide_metal_b200.tokenizer import NativeDecisionTokenizer
+    from test_tokenizer import _synthetic
+    tok = _synthetic(seed=4)
+    tok.save(str(tmp_path / "tokenizer.json"))
+    (tmp_path / "tokenizer_config.json").write_text(json.dumps({"tokenizer_class": "DebertaV2Tokenizer"}))
+    nt = NativeDecisionTokenizer(tmp_path)
+    layers, vocab = 2, 4096
+    path, w = weights_file(13, layers, vocab)
+    model = g.GLiNERDecideClassifier(path, configuration=g.DeBERTaV2Configuration(num_hidden_layers=layers,
+                                                                                  vocab_size=vocab))
+    rng = np.random.default_rng(3)
+    words = ["good", "bad", "match", "team", "vote", "price", "rain", "sun", "great", "awful"]
+    ex = []
+    for i in range(12):
+        text = " ".join(rng.choice(words, int(rng.integers(3, 40)))).capitalize()
+        tasks = [g.DecisionTask("sentiment", ("positive", "negative", "neutral"), False),
+                 g.DecisionTask("topic", ("sports", "politics", "weather", "money"), bool(i % 2), prompt="topic")]
+        ex.append(serve.RawExample(f"r{i}", text, tasks[: 1 + i % 2]))
+    res = serve.run_raw_examples(model, nt, ex, batch_size=4)
+    W = rf.OracleWeights(w, rf.OracleConfig(num_hidden_layers=layers, vocab_size=vocab))
+    for r, e in zip(res, ex):
+        inp = nt.make_input(e.text, e.tasks)
+        ref = rf.forward(W, inp.input_ids, inp.attention_mask, inp.marker_indices, inp.marker_mask)[0]
+        dec = rf.decode(ref, [len(t.labels) for t in e.tasks], [t.multi_label for t in e.tasks])
+        assert [p.task for p in r.predictions] == [t.name for t in e.tasks]
+        for p, t, (pr, _) in zip(r.predictions, e.tasks, dec):
+            np.testing.assert_allclose(p.probabilities, pr[:len(t.labels)], atol=PROB_ATOL, rtol=0)
+    model.close()
