@@ -17,10 +17,39 @@ namespace {
 
 constexpr int kRowsPerBlock = 8;  // 8 warps, one row each
 
+// gamma / beta of this lane's columns. Rows of up to 1024 columns load them before the row,
+// so their round trip overlaps the row's instead of following the statistics; wider rows
+// (more registers per lane) load them where they are used.
 template <int CH>
-__device__ __forceinline__ void ln_row_store(float (&v)[CH * 8], const __half* __restrict__ gamma,
-                                             const __half* __restrict__ beta, __half* __restrict__ dst, int lane,
-                                             float eps, float scale_after) {
+struct AffineRegs {
+  static constexpr bool kEarly = CH <= 4;
+  static constexpr int kN = kEarly ? CH : 1;
+  uint4 g[kN], b[kN];
+  const __half* gamma;
+  const __half* beta;
+  __device__ __forceinline__ void load(const __half* __restrict__ gm, const __half* __restrict__ bt, int lane) {
+    gamma = gm;
+    beta = bt;
+    if (kEarly) {
+#pragma unroll
+      for (int c = 0; c < kN; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        g[c] = __ldg(reinterpret_cast<const uint4*>(gamma + col));
+        b[c] = __ldg(reinterpret_cast<const uint4*>(beta + col));
+      }
+    }
+  }
+  __device__ __forceinline__ uint4 gv(int c, int col) const {
+    return kEarly ? g[c < kN ? c : 0] : __ldg(reinterpret_cast<const uint4*>(gamma + col));
+  }
+  __device__ __forceinline__ uint4 bv(int c, int col) const {
+    return kEarly ? b[c < kN ? c : 0] : __ldg(reinterpret_cast<const uint4*>(beta + col));
+  }
+};
+
+template <int CH>
+__device__ __forceinline__ void ln_row_store(float (&v)[CH * 8], const AffineRegs<CH>& aff, __half* __restrict__ dst,
+                                             int lane, float eps, float scale_after) {
   constexpr int cols = CH * 256;
   float s = 0.f;
 #pragma unroll
@@ -37,10 +66,10 @@ __device__ __forceinline__ void ln_row_store(float (&v)[CH * 8], const __half* _
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
     const int col = (c * 32 + lane) * 8;
-    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gamma + col));
-    const uint4 bv = __ldg(reinterpret_cast<const uint4*>(beta + col));
-    const __half2* gh = reinterpret_cast<const __half2*>(&gv);
-    const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+    const uint4 gw = aff.gv(c, col);
+    const uint4 bw = aff.bv(c, col);
+    const __half2* gh = reinterpret_cast<const __half2*>(&gw);
+    const __half2* bh = reinterpret_cast<const __half2*>(&bw);
     uint32_t o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -68,6 +97,8 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
   if (row >= rows || (m_dev != nullptr && row >= *m_dev)) return;
+  AffineRegs<CH> aff;
+  aff.load(gamma, beta, lane);
   const __half* xr = x + row * cols;
   float v[CH * 8];
 #pragma unroll
@@ -93,7 +124,7 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
       }
     }
   }
-  ln_row_store<CH>(v, gamma, beta, out + row * cols, lane, eps, 1.0f);
+  ln_row_store<CH>(v, aff, out + row * cols, lane, eps, 1.0f);
 }
 
 template <int CH>
@@ -106,6 +137,8 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
   if (row >= rows || (m_dev != nullptr && row >= *m_dev)) return;
+  AffineRegs<CH> aff;
+  aff.load(gamma, beta, lane);
   const long long src = rowmap != nullptr ? (long long)rowmap[row] : row;  // dense position of the row
   long long id = ids[src];
   if (id < 0 || id >= vocab) {
@@ -128,7 +161,7 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
   }
   const float m = __half2float(mask[src]);
   // scale_after == 1 would skip the rounding; a mask of exactly 1 changes nothing anyway.
-  ln_row_store<CH>(v, gamma, beta, out + row * cols, lane, eps, m);
+  ln_row_store<CH>(v, aff, out + row * cols, lane, eps, m);
 }
 
 }  // namespace
