@@ -132,7 +132,7 @@ def _classify(models, inp: DecisionInput) -> Tuple[np.ndarray, float]:
 
 
 def run_examples(models, examples: Sequence[TokenizedExample], buckets=DEFAULT_BUCKETS,
-                 batch_size: int = 32) -> List[RawResult]:
+                 batch_size: int = 32, group_by: str = "shape") -> List[RawResult]:
     """RawCLI.runJSONL (RawCLI.swift:104-171) from the tokenised rows on: layout each row,
     group by (L, maxHeads, maxOptions), classify in chunks of ``batch_size``, decode."""
     if batch_size <= 0:
@@ -142,11 +142,11 @@ def run_examples(models, examples: Sequence[TokenizedExample], buckets=DEFAULT_B
         t0 = time.perf_counter()
         inp = make_input_from_tokens(ex.token_ids, ex.marker_positions, buckets)
         pending.append(_Pending(i, ex, inp, (time.perf_counter() - t0) * 1e3))
-    return _classify_pending(models, pending, batch_size)
+    return _classify_pending(models, pending, batch_size, group_by)
 
 
 def run_raw_examples(models, tokenizer, examples: Sequence[RawExample], buckets=DEFAULT_BUCKETS,
-                     batch_size: int = 32) -> List[RawResult]:
+                     batch_size: int = 32, group_by: str = "shape") -> List[RawResult]:
     """RawCLI.runJSONL (RawCLI.swift:104-171) from the raw text: ``makeInput`` per row (its
     time is the row's preprocessing), then grouping, chunking and decoding as above."""
     if batch_size <= 0:
@@ -156,19 +156,40 @@ def run_raw_examples(models, tokenizer, examples: Sequence[RawExample], buckets=
         t0 = time.perf_counter()
         inp = tokenizer.make_input(ex.text, ex.tasks, buckets)
         pending.append(_Pending(i, ex, inp, (time.perf_counter() - t0) * 1e3))
-    return _classify_pending(models, pending, batch_size)
+    return _classify_pending(models, pending, batch_size, group_by)
 
 
-def _classify_pending(models, pending: Sequence["_Pending"], batch_size: int) -> List[RawResult]:
-    groups: Dict[Tuple[int, int, int], List[_Pending]] = {}
+def _pad_markers(inp: DecisionInput, hm: int, o: int) -> DecisionInput:
+    """Marker arrays widened to [1, hm, o]; the new slots have mask 0 (logit -10000, never
+    decoded), so the row's own logits do not change."""
+    _, _, h0, o0 = inp.shape
+    if (h0, o0) == (hm, o):
+        return inp
+    mi = np.zeros((1, hm, o), inp.marker_indices.dtype)
+    mm = np.zeros((1, hm, o), inp.marker_mask.dtype)
+    mi[:, :h0, :o0] = inp.marker_indices
+    mm[:, :h0, :o0] = inp.marker_mask
+    return DecisionInput(inp.input_ids, inp.attention_mask, mi, mm)
+
+
+def _classify_pending(models, pending: Sequence["_Pending"], batch_size: int,
+                      group_by: str = "shape") -> List[RawResult]:
+    """Groups by (L, maxHeads, maxOptions) as RawCLI does (``group_by="shape"``), or by the
+    bucket length alone with each chunk's marker arrays widened to its largest task / label
+    counts (``"length"``: fewer, fuller batches; every row's logits are the same)."""
+    if group_by not in ("shape", "length"):
+        raise ValueError(f"group_by must be 'shape' or 'length', got {group_by!r}")
+    groups: Dict[Tuple[int, ...], List[_Pending]] = {}
     for p in pending:
         _, L, hm, o = p.input.shape
-        groups.setdefault((L, hm, o), []).append(p)
+        groups.setdefault((L, hm, o) if group_by == "shape" else (L,), []).append(p)
     results: List[RawResult] = [None] * len(pending)  # type: ignore[list-item]
     for group in groups.values():
         for start in range(0, len(group), batch_size):
             batch = group[start:start + batch_size]
-            inp = DecisionInput.concatenated([p.input for p in batch])
+            hm = max(p.input.shape[2] for p in batch)
+            o = max(p.input.shape[3] for p in batch)
+            inp = DecisionInput.concatenated([_pad_markers(p.input, hm, o) for p in batch])
             logits, ms = _classify(models, inp)
             for row, p in enumerate(batch):
                 results[p.index] = RawResult(p.example.id, decode(logits, p.example.tasks, row), p.preprocessing_ms,
@@ -197,6 +218,9 @@ def main(argv=None) -> int:
                                                        "--jsonl lines are RawExample {id, text, tasks}")
     ap.add_argument("--buckets", default=",".join(str(b) for b in DEFAULT_BUCKETS))
     ap.add_argument("--batch-size", type=int, default=32)
+    ap.add_argument("--group-by", choices=("length", "shape"), default="length",
+                    help="batch rows of one bucket length (marker slots widened) or of one "
+                         "(L, maxHeads, maxOptions) shape as RawCLI")
     ap.add_argument("--devices", default="0", help="comma-separated CUDA devices; rows of a chunk are split")
     ap.add_argument("--layers", type=int, default=24, help="encoder layers in the weights file")
     ap.add_argument("--vocab", type=int, default=128011)
@@ -214,12 +238,12 @@ def main(argv=None) -> int:
             examples = load_raw_jsonl(args.jsonl)
 
             def run(rows):
-                return run_raw_examples(models, tok, rows, buckets, args.batch_size)
+                return run_raw_examples(models, tok, rows, buckets, args.batch_size, args.group_by)
         else:
             examples = load_jsonl(args.jsonl) if args.jsonl else synthetic_examples(args.synthetic_rows, buckets)
 
             def run(rows):
-                return run_examples(models, rows, buckets, args.batch_size)
+                return run_examples(models, rows, buckets, args.batch_size, args.group_by)
         print(f"loaded {len(examples)} examples", file=sys.stderr)
         run(examples[:min(len(examples), args.batch_size)])  # warm-up
         t0 = time.perf_counter()

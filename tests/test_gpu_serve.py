@@ -14,7 +14,8 @@ LOGIT_ATOL = 2e-2
 PROB_ATOL = 1e-3
 
 
-def test_config3_serving_loop_matches_oracle(weights_file):
+@pytest.mark.parametrize("group_by", ["shape", "length"])
+def test_config3_serving_loop_matches_oracle(weights_file, group_by):
     import gliner_decide_metal_b200 as g
     from gliner_decide_metal_b200 import serve, synthetic
     layers, vocab = 2, 128011
@@ -26,7 +27,7 @@ def test_config3_serving_loop_matches_oracle(weights_file):
         tasks = [g.DecisionTask(f"t{h}", tuple(f"l{j}" for j in range(n)), m) for h, (n, m) in
                  enumerate(zip(n_labels, ml))]
         ex.append(serve.TokenizedExample(f"r{i}", [int(x) for x in ids], tasks, [list(p) for p in markers]))
-    res = serve.run_examples(model, ex, batch_size=8)
+    res = serve.run_examples(model, ex, batch_size=8, group_by=group_by)
     W = rf.OracleWeights(w, rf.OracleConfig(num_hidden_layers=layers, vocab_size=vocab))
     buckets = set()
     for r, e in zip(res, ex):

@@ -77,3 +77,18 @@ def test_jsonl_round_trip_and_output_format(tmp_path):
     assert set(out[0]) == {"id", "predictions", "preprocessingMilliseconds", "inferenceMilliseconds"}
     assert set(out[0]["predictions"][0]) == {"task", "labels", "probabilities"}
     json.dumps(out)
+
+
+def test_group_by_length_gives_the_same_predictions():
+    """Batching rows of one bucket length with widened marker arrays: fewer batches, the
+    same predictions and probabilities for every row."""
+    ex = _examples(60, seed=7)
+    m1, m2 = _FakeModel(), _FakeModel()
+    by_shape = serve.run_examples(m1, ex, batch_size=8)
+    by_len = serve.run_examples(m2, ex, batch_size=8, group_by="length")
+    assert len(m2.batches) < len(m1.batches)
+    assert {L for _, L, _, _ in m2.batches} == {L for _, L, _, _ in m1.batches}
+    for a, b in zip(by_shape, by_len):
+        assert a.id == b.id
+        assert [(p.task, p.labels, p.probabilities) for p in a.predictions] == \
+            [(p.task, p.labels, p.probabilities) for p in b.predictions]
