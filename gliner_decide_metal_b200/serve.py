@@ -172,24 +172,52 @@ def _pad_markers(inp: DecisionInput, hm: int, o: int) -> DecisionInput:
     return DecisionInput(inp.input_ids, inp.attention_mask, mi, mm)
 
 
+def _pad_length(inp: DecisionInput, L: int, pad_id: int = 0) -> DecisionInput:
+    """A row padded to a longer bucket: [PAD] ids and mask 0 past its own bucket. A padded
+    position is only a masked key, so the row's logits do not change."""
+    L0 = inp.shape[1]
+    if L0 == L:
+        return inp
+    ids = np.full((1, L), pad_id, inp.input_ids.dtype)
+    mask = np.zeros((1, L), inp.attention_mask.dtype)
+    ids[:, :L0] = inp.input_ids
+    mask[:, :L0] = inp.attention_mask
+    return DecisionInput(ids, mask, inp.marker_indices, inp.marker_mask)
+
+
 def _classify_pending(models, pending: Sequence["_Pending"], batch_size: int,
                       group_by: str = "shape") -> List[RawResult]:
-    """Groups by (L, maxHeads, maxOptions) as RawCLI does (``group_by="shape"``), or by the
-    bucket length alone with each chunk's marker arrays widened to its largest task / label
-    counts (``"length"``: fewer, fuller batches; every row's logits are the same)."""
-    if group_by not in ("shape", "length"):
-        raise ValueError(f"group_by must be 'shape' or 'length', got {group_by!r}")
+    """Batches the rows:
+    * ``"shape"``: by (L, maxHeads, maxOptions), as RawCLI does;
+    * ``"length"``: by bucket length, each chunk's marker arrays widened to its largest
+      task / label counts;
+    * ``"stream"``: in input order, each chunk padded to the bucket of its longest row and
+      every chunk's marker arrays to the largest counts of the whole input (with packed
+      encoder rows a row costs the same in any bucket; one batch shape, full batches).
+    Every row's logits are the same in all three (added marker slots have mask 0, added
+    positions are masked keys)."""
+    if group_by not in ("shape", "length", "stream"):
+        raise ValueError(f"group_by must be 'shape', 'length' or 'stream', got {group_by!r}")
     groups: Dict[Tuple[int, ...], List[_Pending]] = {}
     for p in pending:
         _, L, hm, o = p.input.shape
-        groups.setdefault((L, hm, o) if group_by == "shape" else (L,), []).append(p)
+        key = (L, hm, o) if group_by == "shape" else ((L,) if group_by == "length" else ())
+        groups.setdefault(key, []).append(p)
     results: List[RawResult] = [None] * len(pending)  # type: ignore[list-item]
+    hm_all = max((p.input.shape[2] for p in pending), default=1)
+    o_all = max((p.input.shape[3] for p in pending), default=1)
     for group in groups.values():
         for start in range(0, len(group), batch_size):
             batch = group[start:start + batch_size]
-            hm = max(p.input.shape[2] for p in batch)
-            o = max(p.input.shape[3] for p in batch)
-            inp = DecisionInput.concatenated([_pad_markers(p.input, hm, o) for p in batch])
+            if group_by == "stream":
+                hm, o = hm_all, o_all
+                L = max(p.input.shape[1] for p in batch)
+                rows = [_pad_length(_pad_markers(p.input, hm, o), L) for p in batch]
+            else:
+                hm = max(p.input.shape[2] for p in batch)
+                o = max(p.input.shape[3] for p in batch)
+                rows = [_pad_markers(p.input, hm, o) for p in batch]
+            inp = DecisionInput.concatenated(rows)
             logits, ms = _classify(models, inp)
             for row, p in enumerate(batch):
                 results[p.index] = RawResult(p.example.id, decode(logits, p.example.tasks, row), p.preprocessing_ms,
@@ -218,9 +246,10 @@ def main(argv=None) -> int:
                                                        "--jsonl lines are RawExample {id, text, tasks}")
     ap.add_argument("--buckets", default=",".join(str(b) for b in DEFAULT_BUCKETS))
     ap.add_argument("--batch-size", type=int, default=32)
-    ap.add_argument("--group-by", choices=("length", "shape"), default="length",
-                    help="batch rows of one bucket length (marker slots widened) or of one "
-                         "(L, maxHeads, maxOptions) shape as RawCLI")
+    ap.add_argument("--group-by", choices=("stream", "length", "shape"), default="stream",
+                    help="stream: rows in input order, each chunk at its longest row's bucket; "
+                         "length: rows of one bucket length; shape: one (L, maxHeads, maxOptions) "
+                         "shape per batch as RawCLI")
     ap.add_argument("--devices", default="0", help="comma-separated CUDA devices; rows of a chunk are split")
     ap.add_argument("--layers", type=int, default=24, help="encoder layers in the weights file")
     ap.add_argument("--vocab", type=int, default=128011)

@@ -14,7 +14,7 @@ LOGIT_ATOL = 2e-2
 PROB_ATOL = 1e-3
 
 
-@pytest.mark.parametrize("group_by", ["shape", "length"])
+@pytest.mark.parametrize("group_by", ["shape", "length", "stream"])
 def test_config3_serving_loop_matches_oracle(weights_file, group_by):
     import gliner_decide_metal_b200 as g
     from gliner_decide_metal_b200 import serve, synthetic

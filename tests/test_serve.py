@@ -92,3 +92,18 @@ def test_group_by_length_gives_the_same_predictions():
         assert a.id == b.id
         assert [(p.task, p.labels, p.probabilities) for p in a.predictions] == \
             [(p.task, p.labels, p.probabilities) for p in b.predictions]
+
+
+def test_group_by_stream_pads_chunks_and_keeps_predictions():
+    """Rows in input order, each chunk at its longest row's bucket with the marker arrays of
+    the whole input: one batch per chunk, the same predictions for every row."""
+    ex = _examples(50, seed=9)
+    m1, m2 = _FakeModel(), _FakeModel()
+    by_shape = serve.run_examples(m1, ex, batch_size=8)
+    by_stream = serve.run_examples(m2, ex, batch_size=8, group_by="stream")
+    assert len(m2.batches) == 7 and [b for b, *_ in m2.batches] == [8] * 6 + [2]
+    assert len({(hm, o) for _, _, hm, o in m2.batches}) == 1
+    for a, b in zip(by_shape, by_stream):
+        assert a.id == b.id
+        assert [(p.task, p.labels, p.probabilities) for p in a.predictions] == \
+            [(p.task, p.labels, p.probabilities) for p in b.predictions]
