@@ -45,7 +45,8 @@ from typing import Dict, List, Sequence, Tuple
 import numpy as np
 
 from . import (DEFAULT_BUCKETS, DecisionInput, DecisionTask, DeBERTaV2Configuration, GLiNERDecideClassifier,
-               Prediction, classify_sharded, decode, make_input_from_tokens)
+               InputDoesNotFitError, NoTaskLabelsError, Prediction, classify_sharded, decode, decode_batch,
+               make_input_from_tokens)
 
 
 @dataclass
@@ -131,12 +132,76 @@ def _classify(models, inp: DecisionInput) -> Tuple[np.ndarray, float]:
     return logits, (time.perf_counter() - t0) * 1e3
 
 
+def _decode_chunk(logits: np.ndarray, tasks_per_row: Sequence[Sequence[DecisionTask]]) -> List[List[Prediction]]:
+    """``decode`` (RawCLI.swift:182-223) of a whole chunk with one ``gdc_decode`` call."""
+    B, hm, _ = logits.shape
+    nl = np.zeros((B, hm), np.int32)
+    ml = np.zeros((B, hm), np.uint8)
+    for r, tasks in enumerate(tasks_per_row):
+        for h, t in enumerate(tasks):
+            nl[r, h] = len(t.labels)
+            ml[r, h] = int(t.multi_label)
+    probs, sel = decode_batch(logits, nl, ml)
+    out = []
+    for r, tasks in enumerate(tasks_per_row):
+        preds = []
+        for h, t in enumerate(tasks):
+            n = len(t.labels)
+            preds.append(Prediction(t.name, [t.labels[i] for i in range(n) if sel[r, h, i]], probs[r, h, :n].tolist()))
+        out.append(preds)
+    return out
+
+
+def _run_stream_tokens(models, examples: Sequence[TokenizedExample], buckets, batch_size: int) -> List[RawResult]:
+    """``group_by="stream"`` over tokenised rows with the layout of ``gdc_layout_row``
+    (NativeTokenizer.swift:134-157: smallest bucket, [PAD]=0 padding, mask, markers
+    [h * O + o] for o < O) written for a whole chunk at once; each row's preprocessing time is
+    its share of its chunk's layout time."""
+    order = sorted(set(int(b) for b in buckets))
+    if not order:
+        raise InputDoesNotFitError(4, f"Encoded schema/text does not fit any requested bucket: {list(buckets)}")
+    rows_L = []
+    for ex in examples:
+        if not ex.marker_positions or any(len(m) == 0 for m in ex.marker_positions):
+            raise NoTaskLabelsError(5, "Every decision task must contain at least one label")
+        n = len(ex.token_ids)
+        L = next((b for b in order if b >= n), None)
+        if L is None:
+            raise InputDoesNotFitError(4, f"Encoded schema/text does not fit any requested bucket: {order}")
+        rows_L.append(L)
+    hm = max((len(ex.marker_positions) for ex in examples), default=1)
+    o = max((len(m) for ex in examples for m in ex.marker_positions), default=1)
+    results: List[RawResult] = []
+    for start in range(0, len(examples), batch_size):
+        chunk = examples[start:start + batch_size]
+        t0 = time.perf_counter()
+        B, L = len(chunk), max(rows_L[start:start + batch_size])
+        ids = np.zeros((B, L), np.int64)
+        mask = np.zeros((B, L), np.float16)
+        mi = np.zeros((B, hm, o), np.int64)
+        mm = np.zeros((B, hm, o), np.float32)
+        for r, ex in enumerate(chunk):
+            n = len(ex.token_ids)
+            ids[r, :n] = ex.token_ids
+            mask[r, :n] = 1
+            for h, pos in enumerate(ex.marker_positions):
+                mi[r, h, :len(pos)] = pos
+                mm[r, h, :len(pos)] = 1
+        prep_ms = (time.perf_counter() - t0) * 1e3 / B
+        logits, ms = _classify(models, DecisionInput(ids, mask, mi, mm))
+        for ex, preds in zip(chunk, _decode_chunk(logits, [ex.tasks for ex in chunk])):
+            results.append(RawResult(ex.id, preds, prep_ms, ms / B))
+    return results
+
+
 def run_examples(models, examples: Sequence[TokenizedExample], buckets=DEFAULT_BUCKETS,
                  batch_size: int = 32, group_by: str = "shape") -> List[RawResult]:
     """RawCLI.runJSONL (RawCLI.swift:104-171) from the tokenised rows on: layout each row,
     group by (L, maxHeads, maxOptions), classify in chunks of ``batch_size``, decode."""
     if batch_size <= 0:
         raise ValueError("batch_size must be positive")
+    if group_by == "stream":
+        return _run_stream_tokens(models, examples, buckets, batch_size)
     pending: List[_Pending] = []
     for i, ex in enumerate(examples):
         t0 = time.perf_counter()
@@ -219,9 +284,8 @@ def _classify_pending(models, pending: Sequence["_Pending"], batch_size: int,
                 rows = [_pad_markers(p.input, hm, o) for p in batch]
             inp = DecisionInput.concatenated(rows)
             logits, ms = _classify(models, inp)
-            for row, p in enumerate(batch):
-                results[p.index] = RawResult(p.example.id, decode(logits, p.example.tasks, row), p.preprocessing_ms,
-                                             ms / len(batch))
+            for p, preds in zip(batch, _decode_chunk(logits, [p.example.tasks for p in batch])):
+                results[p.index] = RawResult(p.example.id, preds, p.preprocessing_ms, ms / len(batch))
     return results
 
 

@@ -107,3 +107,43 @@ def test_group_by_stream_pads_chunks_and_keeps_predictions():
         assert a.id == b.id
         assert [(p.task, p.labels, p.probabilities) for p in a.predictions] == \
             [(p.task, p.labels, p.probabilities) for p in b.predictions]
+
+
+def test_stream_layout_matches_gdc_layout_row():
+    """The stream path's chunk layout equals make_input_from_tokens (gdc_layout_row) row by
+    row, padded to the chunk's bucket and the input's marker counts."""
+    ex = _examples(70, seed=12)
+    model = _FakeModel()
+    captured = []
+    orig = model.classify
+
+    def spy(inp):
+        captured.append(inp)
+        return orig(inp)
+    model.classify = spy
+    serve.run_examples(model, ex, batch_size=16, group_by="stream")
+    k = 0
+    for inp in captured:
+        B, L, hm, o = inp.shape
+        for r in range(B):
+            one = g.make_input_from_tokens(ex[k].token_ids, ex[k].marker_positions)
+            _, L1, h1, o1 = one.shape
+            assert L1 <= L and h1 <= hm and o1 <= o
+            assert np.array_equal(inp.input_ids[r, :L1], one.input_ids[0])
+            assert (inp.input_ids[r, L1:] == 0).all() and (inp.attention_mask[r, L1:] == 0).all()
+            assert np.array_equal(inp.attention_mask[r, :L1], one.attention_mask[0])
+            assert np.array_equal(inp.marker_indices[r, :h1, :o1], one.marker_indices[0])
+            assert np.array_equal(inp.marker_mask[r, :h1, :o1], one.marker_mask[0])
+            assert inp.marker_mask[r, h1:].sum() == 0 and inp.marker_mask[r, :, o1:].sum() == 0
+            k += 1
+    assert k == len(ex)
+
+
+def test_stream_errors_match_layout_errors():
+    import pytest
+    ex = _examples(3)
+    bad = serve.TokenizedExample("x", ex[0].token_ids, ex[0].tasks, [[]])
+    with pytest.raises(g.NoTaskLabelsError):
+        serve.run_examples(_FakeModel(), [bad], group_by="stream")
+    with pytest.raises(g.InputDoesNotFitError):
+        serve.run_examples(_FakeModel(), ex, buckets=[8], group_by="stream")
