@@ -38,11 +38,13 @@ gdc_status launch_residual_layer_norm(const __half* x, const __half* residual, c
 
 // hidden[t] = LN(E[ids[t]]) * mask[t] for t < rows (DeBERTa.swift:285-292). Ids outside
 // [0, vocab) set kErrBadTokenId and read row 0. Packed rows (rowmap and m_dev non-null):
-// hidden[r] = LN(E[ids[rowmap[r]]]) * mask[rowmap[r]] for r < *m_dev.
+// hidden[r] = LN(E[ids[rowmap[r]]]) * mask[rowmap[r]] for r < *m_dev, and the 256 rows after
+// *m_dev (below `rows`) of hidden and of tail_buf (rows of tail_cols columns, nullable) are
+// zeroed.
 gdc_status launch_embedding(const int32_t* ids, const __half* mask, const __half* table, int64_t vocab,
                             const __half* gamma, const __half* beta, __half* out, int64_t rows, int cols,
                             float eps, cudaStream_t stream, int* err, const int32_t* rowmap = nullptr,
-                            const int32_t* m_dev = nullptr);
+                            const int32_t* m_dev = nullptr, __half* tail_buf = nullptr, int tail_cols = 0);
 
 // Packed-row layout of a batch (pack.cu): seq_off[0..B] (exclusive prefix sum of the
 // per-row extents; seq_off[B] = packed row count), rowmap[r] = b * L + t for packed row

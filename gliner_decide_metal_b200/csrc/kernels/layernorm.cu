@@ -16,6 +16,7 @@ namespace gdc {
 namespace {
 
 constexpr int kRowsPerBlock = 8;  // 8 warps, one row each
+constexpr int kPackedTailRows = 256;  // a GEMM tile (256 rows) covers every row a key tile reaches
 
 // gamma / beta of this lane's columns. Rows of up to 1024 columns load them before the row,
 // so their round trip overlaps the row's instead of following the statistics; wider rows
@@ -132,11 +133,25 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
     embedding_kernel(const int32_t* __restrict__ ids, const __half* __restrict__ mask, const __half* __restrict__ table,
                      long long vocab, const __half* __restrict__ gamma, const __half* __restrict__ beta,
                      __half* __restrict__ out, long long rows, float eps, int* err,
-                     const int32_t* __restrict__ rowmap, const int32_t* __restrict__ m_dev) {
+                     const int32_t* __restrict__ rowmap, const int32_t* __restrict__ m_dev,
+                     __half* __restrict__ tail_buf, int tail_cols) {
   constexpr int cols = CH * 256;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
-  if (row >= rows || (m_dev != nullptr && row >= *m_dev)) return;
+  if (row >= rows) return;
+  if (m_dev != nullptr && row >= *m_dev) {
+    // Rows just past the packed count: GEMM tiles and attention key tiles read them. Zero
+    // hidden rows make every layer's QKV rows there its bias, and zero QKV rows beyond the
+    // last GEMM tile stay zero, so nothing left by an earlier call can reach this one.
+    if (row < (long long)*m_dev + kPackedTailRows) {
+      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+      for (int c = lane; c < cols / 8; c += 32) reinterpret_cast<uint4*>(out + row * cols)[c] = z;
+      if (tail_buf != nullptr)
+        for (int c = lane; c < tail_cols / 8; c += 32)
+          reinterpret_cast<uint4*>(tail_buf + row * (long long)tail_cols)[c] = z;
+    }
+    return;
+  }
   AffineRegs<CH> aff;
   aff.load(gamma, beta, lane);
   const long long src = rowmap != nullptr ? (long long)rowmap[row] : row;  // dense position of the row
@@ -191,15 +206,17 @@ gdc_status launch_residual_layer_norm(const __half* x, const __half* residual, c
 gdc_status launch_embedding(const int32_t* ids, const __half* mask, const __half* table, int64_t vocab,
                             const __half* gamma, const __half* beta, __half* out, int64_t rows, int cols,
                             float eps, cudaStream_t stream, int* err, const int32_t* rowmap,
-                            const int32_t* m_dev) {
+                            const int32_t* m_dev, __half* tail_buf, int tail_cols) {
   if (rows <= 0) return GDC_OK;
   if (cols <= 0 || cols % 256 != 0 || cols > 4096)
     return set_error(GDC_ERR_UNSUPPORTED, "embedding: cols=%d unsupported", cols);
   if ((rowmap == nullptr) != (m_dev == nullptr))
     return set_error(GDC_ERR_INVALID_INPUT, "embedding: rowmap and row count go together");
+  if (tail_buf != nullptr && (tail_cols <= 0 || tail_cols % 8 != 0 || (reinterpret_cast<uintptr_t>(tail_buf) & 15)))
+    return set_error(GDC_ERR_INVALID_INPUT, "embedding: tail buffer must be 16-byte aligned rows of 8k columns");
   const unsigned grid = unsigned((rows + kRowsPerBlock - 1) / kRowsPerBlock);
   GDC_LN_DISPATCH(cols / 256, embedding_kernel, ids, mask, table, (long long)vocab, gamma, beta, out,
-                  (long long)rows, eps, err, rowmap, m_dev);
+                  (long long)rows, eps, err, rowmap, m_dev, tail_buf, tail_cols);
   return check_launch("embedding_kernel");
 }
 

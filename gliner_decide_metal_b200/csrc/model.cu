@@ -314,10 +314,10 @@ gdc_status ensure_workspace(gdc_model* m, int64_t tokens, int64_t markers) {
     GDC_TRY(grow((void**)&w.row_order, size_t(cap) * 4));
     if (!w.ctrl) GDC_TRY(grow((void**)&w.ctrl, 64 * 4));
     GDC_CUDA_TRY(cudaMemsetAsync(w.ctrl, 0, 64 * 4, m->stream));
-    // With packed rows, GEMM tiles and attention key tiles also read rows past the packed
-    // count that no kernel of this call wrote. Starting every activation buffer at zero keeps
-    // such rows finite (later they hold finite values of earlier calls), so a masked key's
-    // zero probability never meets an Inf or NaN value row.
+    // With packed rows, GEMM tiles also read rows past the packed count that no kernel of the
+    // call writes (their outputs are never read). Starting every activation buffer at zero
+    // keeps them finite; the rows attention reads past the count are zeroed by the embedding
+    // kernel on every call.
     for (void* p : {(void*)w.x, (void*)w.x1, (void*)w.ctx, (void*)w.tmp})
       GDC_CUDA_TRY(cudaMemsetAsync(p, 0, size_t(cap) * E * 2, m->stream));
     GDC_CUDA_TRY(cudaMemsetAsync(w.big, 0, size_t(cap) * big_cols * 2, m->stream));
@@ -400,7 +400,7 @@ gdc_status enqueue_forward(gdc_model* m, int B, int L, int Hm, int O, const int3
     work.groups = w.ctrl + 8;
   }
   GDC_TRY(launch_embedding(ids, mask, m->word_emb, m->vocab, m->emb_ln_g, m->emb_ln_b, w.x, T, E, m->eps, s, m->err,
-                           rowmap, m_dev));
+                           rowmap, m_dev, pack ? w.big : nullptr, 3 * E));
   rec.end(kProfEmbedding, "embedding");
   for (int i = 0; i < m->layers_n; ++i) {
     const LayerWeights& Lw = m->layers[size_t(i)];
