@@ -292,11 +292,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kRowWarps + 1) {
     // ------------------------------------------------------------ TMA producer warp
-    // Walks the same (item, key tile) sequence as the MMA issuer and the row warps and
-    // loads each pair's K / V tile (double-buffered) and PK / PQ windows, plus Q per item,
-    // as soon as their buffers are free: the windows and Q once the previous pair's
-    // gathers are done (its probabilities are written), the K / V buffer once PV of the
-    // pair two back has completed. It also publishes each item's key-tile mask.
+    // Picks the work items (from the launch's counter, or every gridDim.x-th) and publishes
+    // each one with its key-tile mask, extent, first qkv row and additive key mask; loads each
+    // pair's K / V tile (double-buffered) and PK / PQ windows, plus Q per item, as soon as
+    // their buffers are free: the windows and Q once the previous pair's gathers are done
+    // (kBarScored, before its exp phase), the K / V buffer once PV of the pair two back has
+    // completed.
     uint8_t* sQ = sm + kOffQ;
     uint8_t* sPK = sm + kOffW;
     uint8_t* sPQ = sm + kOffW + 32768;
