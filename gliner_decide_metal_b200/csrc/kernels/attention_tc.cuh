@@ -8,10 +8,14 @@
 //   ctx[q]   = softmax_k(s) . V
 // with i(r) = clip(bucket(r) + 256, 0, 511) from the 1023-entry table.
 //
-// Persistent: one CTA per SM walks work items (128-query tile, h, b) and, inside an item,
-// the 128-key tiles of the row (tiles whose keys are all padding are skipped: their
-// softmax weight is exactly zero). For a (query tile, key tile) pair the distances q-k
-// span 255 values, so the needed position rows form one window [lo, lo+256) of PQ / PK.
+// Persistent: one CTA per SM takes work items (128-query tile, h, b) one at a time (from an
+// atomic counter, heaviest first, or a static split; see Schedule) and, inside an item,
+// walks the 128-key tiles of the row (tiles whose keys are all padding are skipped: their
+// softmax weight is exactly zero). With packed rows (Schedule::seq_off) a batch row's
+// positions sit at rows seq_off[b] + t of qkv / ctx, query tiles past its extent are never
+// handed out and keys past it get weight zero. For a (query tile, key tile) pair the
+// distances q-k span 255 values, so the needed position rows form one window
+// [lo, lo+256) of PQ / PK.
 // Per pair:
 //   TMA   K, V tiles [128 x 64] (double-buffered) and the PK / PQ windows [256 x 64];
 //         Q [128 x 64] once per item. The next pair's loads (possibly of the next item)
