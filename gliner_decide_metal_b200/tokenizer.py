@@ -20,15 +20,19 @@ The Unigram part (``UnigramTokenizer``) follows the tokenizers-library algorithm
 format defines: the normalizer and pre-tokenizer chain of the file, then a Viterbi search
 for the segmentation with the largest sum of piece scores; a character no piece covers
 becomes an unknown node scored ``min(score) - 10``, and runs of unknown nodes fuse into one
-``unk_id``. ``Precompiled`` normalizers (SentencePiece character maps) are applied as NFKC,
-which agrees with them on ASCII and common text. The checkpoint's own ``tokenizer.json``
-is not available here; tests pin this implementation to the tokenizers library on
-synthetic vocabularies.
+``unk_id``. ``Precompiled`` normalizers (a SentencePiece character map, DeBERTa-v3's
+``nmt_nfkc``) are applied from the map itself: its double-array trie is searched per
+extended grapheme cluster as the tokenizers library does. The checkpoint's own
+``tokenizer.json`` is not available here; tests pin this implementation to the tokenizers
+library on synthetic vocabularies and on a SentencePiece ``nmt_nfkc`` model trained in the
+test.
 """
 from __future__ import annotations
 
+import base64
 import json
 import re
+import struct
 import unicodedata
 from dataclasses import dataclass
 from pathlib import Path
@@ -47,6 +51,68 @@ class TokenizerFilesError(FileNotFoundError):
 
 # --------------------------------------------------------------------------- normalizers
 
+class PrecompiledCharsMap:
+    """A SentencePiece precompiled character map: a little-endian uint32 trie size, a
+    darts-clone double-array trie over UTF-8 keys (uint32 units), then the replacement
+    strings, each NUL-terminated; a key's value is the offset of its replacement.
+
+    ``normalize`` follows the tokenizers library's ``Precompiled`` normalizer: per extended
+    grapheme cluster, a cluster shorter than 6 bytes is replaced by the replacement of its
+    first (shortest) key prefix if it has one; otherwise each character is replaced by its
+    own, or kept."""
+
+    def __init__(self, blob: bytes):
+        (trie_size,) = struct.unpack_from("<I", blob, 0)
+        self.units = struct.unpack_from(f"<{trie_size // 4}I", blob, 4)
+        self.strings = blob[4 + trie_size:]
+        self._memo: Dict[str, Optional[str]] = {}
+
+    def _first_prefix(self, key: bytes) -> Optional[int]:
+        # darts-clone unit fields: has_leaf = bit 8, value = low 31 bits (leaf units),
+        # label = low 8 bits plus bit 31, offset = (unit >> 10) << ((unit & 0x200) >> 6)
+        units = self.units
+        pos = 0
+        unit = units[pos]
+        pos ^= (unit >> 10) << ((unit & 0x200) >> 6)
+        for c in key:
+            pos ^= c
+            if pos >= len(units):
+                return None
+            unit = units[pos]
+            if (unit & 0x800000FF) != c:
+                return None
+            pos ^= (unit >> 10) << ((unit & 0x200) >> 6)
+            if (unit >> 8) & 1:
+                return units[pos] & 0x7FFFFFFF
+        return None
+
+    def transform(self, chunk: str) -> Optional[str]:
+        hit = self._memo.get(chunk, False)
+        if hit is not False:
+            return hit
+        off = self._first_prefix(chunk.encode("utf-8"))
+        out = None
+        if off is not None:
+            end = self.strings.find(b"\0", off)
+            out = self.strings[off:end if end >= 0 else len(self.strings)].decode("utf-8", errors="replace")
+        self._memo[chunk] = out
+        return out
+
+    def normalize(self, s: str) -> str:
+        import regex  # extended grapheme clusters (\X)
+        out = []
+        for g in regex.findall(r"\X", s):
+            if len(g.encode("utf-8")) < 6:
+                n = self.transform(g)
+                if n is not None:
+                    out.append(n)
+                    continue
+            for ch in g:
+                n = self.transform(ch)
+                out.append(ch if n is None else n)
+        return "".join(out)
+
+
 def _normalizer(spec: Optional[dict]):
     """Callable str -> str for a tokenizers ``normalizer`` entry."""
     if spec is None:
@@ -63,7 +129,11 @@ def _normalizer(spec: Optional[dict]):
     if kind in ("NFKC", "NFC", "NFD", "NFKD"):
         return lambda s: unicodedata.normalize(kind, s)
     if kind == "Precompiled":
-        return lambda s: unicodedata.normalize("NFKC", s)
+        blob = spec.get("precompiled_charsmap")
+        if not blob:
+            return lambda s: s
+        cmap = PrecompiledCharsMap(base64.b64decode(blob))
+        return cmap.normalize
     if kind == "Lowercase":
         return lambda s: s.lower()
     if kind == "Strip":
@@ -277,29 +347,39 @@ class NativeDecisionTokenizer:
             raise TokenizerFilesError(f"Tokenizer directory is missing tokenizer.json/tokenizer_config.json: {d}")
         self.unigram = UnigramTokenizer.from_file(d / "tokenizer.json")
         self.special = dict(self.unigram.added)
+        # Each schema entry (one word of the text, a label, a prompt) is tokenised on its own,
+        # so its ids depend on the entry alone: they are cached (bounded) for the repeated
+        # words of real text.
+        self._cache: Dict[str, List[int]] = {}
+        # earliest match first; at one position the alternation tries longer tokens first
+        self._special_rx = (re.compile("|".join(re.escape(t) for t in sorted(self.special, key=len, reverse=True)))
+                            if self.special else None)
         self.pad_id = self.special.get("[PAD]", self.unigram.pieces.get("[PAD]", (0, 0.0))[0])
 
     def token_ids(self, text: str) -> List[int]:
         """Ids of one schema entry: added tokens matched first (earliest, then longest),
         the text between them through the Unigram model (NativeTokenizer.swift:160-196)."""
+        hit = self._cache.get(text)
+        if hit is not None:
+            return hit
         ids: List[int] = []
         cur = 0
         while cur < len(text):
-            best = None
-            for tok in self.special:
-                at = text.find(tok, cur)
-                if at < 0:
-                    continue
-                if best is None or at < best[0] or (at == best[0] and len(tok) > len(best[1])):
-                    best = (at, tok)
-            if best is None:
-                ids += self.unigram.encode(text[cur:])
+            m = self._special_rx.search(text, cur) if self._special_rx is not None else None
+            if m is None:
+                ids += self._plain(text[cur:])
                 break
-            if best[0] > cur:
-                ids += self.unigram.encode(text[cur:best[0]])
-            ids.append(self.special[best[1]])
-            cur = best[0] + len(best[1])
+            if m.start() > cur:
+                ids += self._plain(text[cur:m.start()])
+            ids.append(self.special[m.group(0)])
+            cur = m.end()
+        if len(self._cache) >= 200_000:
+            self._cache.clear()
+        self._cache[text] = ids
         return ids
+
+    def _plain(self, text: str) -> List[int]:
+        return self.unigram.encode(text)
 
     def encode_schema(self, text: str, tasks: Sequence[DecisionTask]) -> Tuple[List[int], List[List[int]]]:
         """Unpadded ids and, per task, the positions of its label markers."""
@@ -309,7 +389,7 @@ class NativeDecisionTokenizer:
         markers: List[List[int]] = [[] for _ in tasks]
         for entry in schema_entries(text, tasks):
             start = len(ids)
-            ids += self.token_ids(entry.text)
+            ids.extend(self.token_ids(entry.text))
             if entry.label_of is not None:
                 markers[entry.label_of].append(start)
         return ids, markers

@@ -166,3 +166,53 @@ def test_raw_jsonl_parsing_and_layout(tok_dir, tmp_path):
     nt = NativeDecisionTokenizer(d)
     rows = [nt.make_input(e.text, e.tasks) for e in ex]
     assert all(r.shape[2:] == (1, 2) for r in rows)
+
+
+def _spm_tokenizer(tmp_path, seed=0):
+    """A DeBERTa-v3-style tokenizer.json from a SentencePiece unigram model with the nmt_nfkc
+    normalization rule, trained here: the model's pieces and scores, its precompiled
+    character map as a Precompiled normalizer (Strip, Precompiled, collapse spaces as the
+    DeBERTa-v2 conversion writes), Metaspace pre-tokenizer."""
+    spm = pytest.importorskip("sentencepiece")
+    from sentencepiece import sentencepiece_model_pb2 as pb
+    from tokenizers import Regex, Tokenizer, models, normalizers, pre_tokenizers
+    rng = np.random.default_rng(seed)
+    syll = ["ka", "to", "ri", "mu", "sen", "ver", "al", "on", "de", "ba", "qu", "ix", "ph", "str", "ing", "ed",
+            "ly", "tion", "ﬁ", "é", "ü", "ß", "Ω", "½", "①", "ｶ", "中", "文", "é", "Å", "™", "…"]
+    lines = [" ".join("".join(rng.choice(syll, int(rng.integers(1, 4)))) for _ in range(int(rng.integers(5, 20))))
+             for _ in range(3000)]
+    corpus = tmp_path / "corpus.txt"
+    corpus.write_text("\n".join(lines), encoding="utf-8")
+    spm.SentencePieceTrainer.train(input=str(corpus), model_prefix=str(tmp_path / "m"), vocab_size=400,
+                                   model_type="unigram", normalization_rule_name="nmt_nfkc", pad_id=0, unk_id=1,
+                                   bos_id=2, eos_id=3, pad_piece="[PAD]", unk_piece="[UNK]", bos_piece="[CLS]",
+                                   eos_piece="[SEP]", num_threads=1, minloglevel=2)
+    m = pb.ModelProto()
+    m.ParseFromString((tmp_path / "m.model").read_bytes())
+    tok = Tokenizer(models.Unigram([(p.piece, p.score) for p in m.pieces], unk_id=1, byte_fallback=False))
+    tok.normalizer = normalizers.Sequence([normalizers.Strip(),
+                                           normalizers.Precompiled(m.normalizer_spec.precompiled_charsmap),
+                                           normalizers.Replace(Regex(" {2,}"), " ")])
+    tok.pre_tokenizer = pre_tokenizers.Metaspace(replacement="▁", prepend_scheme="always")
+    tok.add_special_tokens(SPECIALS[4:])
+    return tok
+
+
+def test_precompiled_nmt_nfkc_matches_tokenizers_library(tmp_path):
+    """The Precompiled (SentencePiece nmt_nfkc) normalizer and the whole Unigram pipeline
+    against the tokenizers library, on text with ligatures, full-width and circled forms,
+    combining marks, emoji and other non-ASCII."""
+    from gliner_decide_metal_b200.tokenizer import UnigramTokenizer
+    tok = _spm_tokenizer(tmp_path)
+    tok.save(str(tmp_path / "tokenizer.json"))
+    mine = UnigramTokenizer.from_file(tmp_path / "tokenizer.json")
+    rng = np.random.default_rng(7)
+    alphabet = list("abcdefghijklmnopqrstuvwxyzABC  .,") + ["ﬁ", "ﬂ", "é", "é", "Å", "Å", "ü", "ß", "Ω", "Ω",
+                                                           "½", "①", "⑳", "ｶ", "ﾀ", "ｱ", "ｄ", "中", "文", "™", "…",
+                                                           "　", " ", "👍", "👍🏽", "🇩🇪", "​", "ℌ"]
+    texts = ["ﬁne Café ①② ｶﾀｶﾅ  double  space", "été Ångström", "👍🏽 ok 🇩🇪", "½ ™ …"]
+    texts += ["".join(rng.choice(alphabet, int(rng.integers(1, 30)))) for _ in range(400)]
+    for t in texts:
+        assert mine.normalize(t) == tok.normalizer.normalize_str(t), t
+        enc = tok.encode(t, add_special_tokens=False)
+        assert mine.encode(t) == enc.ids, (t, mine.tokenize(t), enc.tokens)
