@@ -216,12 +216,49 @@ def run_raw_examples(models, tokenizer, examples: Sequence[RawExample], buckets=
     time is the row's preprocessing), then grouping, chunking and decoding as above."""
     if batch_size <= 0:
         raise ValueError("batch_size must be positive")
+    if group_by == "stream":
+        return _run_stream_raw(models, tokenizer, examples, buckets, batch_size)
     pending: List[_Pending] = []
     for i, ex in enumerate(examples):
         t0 = time.perf_counter()
         inp = tokenizer.make_input(ex.text, ex.tasks, buckets)
         pending.append(_Pending(i, ex, inp, (time.perf_counter() - t0) * 1e3))
     return _classify_pending(models, pending, batch_size, group_by)
+
+
+def _run_stream_raw(models, tokenizer, examples: Sequence[RawExample], buckets, batch_size: int) -> List[RawResult]:
+    """``group_by="stream"`` from raw text, pipelined: a worker thread tokenises chunk k+1
+    while chunk k is classified (the classify call runs in the C library without the
+    interpreter lock). The marker arrays' width comes from the tasks (tasks per row, labels
+    per task), so every chunk has the same marker shape without tokenising ahead."""
+    from concurrent.futures import ThreadPoolExecutor
+    hm = max((len(ex.tasks) for ex in examples), default=1)
+    o = max((len(t.labels) for ex in examples for t in ex.tasks), default=1)
+
+    def prepare(chunk: Sequence[RawExample]):
+        inputs, prep = [], []
+        for ex in chunk:
+            t0 = time.perf_counter()
+            inputs.append(tokenizer.make_input(ex.text, ex.tasks, buckets))
+            prep.append((time.perf_counter() - t0) * 1e3)
+        L = max(inp.shape[1] for inp in inputs)
+        rows = [_pad_length(_pad_markers(inp, max(hm, inp.shape[2]), max(o, inp.shape[3])), L) for inp in inputs]
+        return DecisionInput.concatenated(rows), prep
+
+    chunks = [examples[i:i + batch_size] for i in range(0, len(examples), batch_size)]
+    results: List[RawResult] = []
+    if not chunks:
+        return results
+    with ThreadPoolExecutor(max_workers=1) as pool:
+        nxt = pool.submit(prepare, chunks[0])
+        for k, chunk in enumerate(chunks):
+            inp, prep = nxt.result()
+            if k + 1 < len(chunks):
+                nxt = pool.submit(prepare, chunks[k + 1])
+            logits, ms = _classify(models, inp)
+            for ex, p_ms, preds in zip(chunk, prep, _decode_chunk(logits, [ex.tasks for ex in chunk])):
+                results.append(RawResult(ex.id, preds, p_ms, ms / len(chunk)))
+    return results
 
 
 def _pad_markers(inp: DecisionInput, hm: int, o: int) -> DecisionInput:

@@ -216,3 +216,28 @@ def test_precompiled_nmt_nfkc_matches_tokenizers_library(tmp_path):
         assert mine.normalize(t) == tok.normalizer.normalize_str(t), t
         enc = tok.encode(t, add_special_tokens=False)
         assert mine.encode(t) == enc.ids, (t, mine.tokenize(t), enc.tokens)
+
+
+def test_raw_stream_pipeline_matches_shape_grouping(tok_dir):
+    """Raw-text rows through the pipelined stream path (tokenising the next chunk while the
+    current one is classified) give the same predictions as RawCLI's shape grouping."""
+    import gliner_decide_metal_b200 as g
+    from gliner_decide_metal_b200 import serve
+    from gliner_decide_metal_b200.tokenizer import NativeDecisionTokenizer
+    from test_serve import _FakeModel
+    d, _ = tok_dir
+    nt = NativeDecisionTokenizer(d)
+    rng = np.random.default_rng(2)
+    words = ["good", "bad", "match", "team", "vote", "price", "rain", "sun"]
+    ex = []
+    for i in range(37):
+        tasks = [g.DecisionTask("s", ("pos", "neg", "neu")), g.DecisionTask("t", ("a", "b", "c", "d", "e"), True)]
+        ex.append(serve.RawExample(f"r{i}", " ".join(rng.choice(words, int(rng.integers(1, 60)))), tasks[: 1 + i % 2]))
+    a = serve.run_raw_examples(_FakeModel(), nt, ex, batch_size=8, group_by="shape")
+    m = _FakeModel()
+    b = serve.run_raw_examples(m, nt, ex, batch_size=8, group_by="stream")
+    assert [x.id for x in b] == [e.id for e in ex]
+    assert len(m.batches) == 5 and len({(hm, o) for _, _, hm, o in m.batches}) == 1
+    for x, y in zip(a, b):
+        assert [(p.task, p.labels, p.probabilities) for p in x.predictions] == \
+            [(p.task, p.labels, p.probabilities) for p in y.predictions]
