@@ -45,7 +45,7 @@ from typing import Dict, List, Sequence, Tuple
 import numpy as np
 
 from . import (DEFAULT_BUCKETS, DecisionInput, DecisionTask, DeBERTaV2Configuration, GLiNERDecideClassifier,
-               InputDoesNotFitError, NoTaskLabelsError, Prediction, classify_sharded, decode, decode_batch,
+               InputDoesNotFitError, NoTaskLabelsError, Prediction, classify_sharded, decode_batch,
                make_input_from_tokens)
 
 

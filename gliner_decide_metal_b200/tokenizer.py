@@ -38,7 +38,6 @@ from dataclasses import dataclass
 from pathlib import Path
 from typing import Dict, List, Optional, Sequence, Tuple
 
-import numpy as np
 
 from . import DEFAULT_BUCKETS, DecisionInput, DecisionTask, NoTaskLabelsError, make_input_from_tokens
 
