@@ -161,6 +161,27 @@ def test_model_load_error_codes(tmp_path):
     st, msg = _load_status(p)
     assert st == 6 and "truncated" in msg
 
+    # a weight of the right shape stored as an integer type -> invalid shape (not a float type)
+    import json as _json
+    p = tmp_path / "dtype.safetensors"
+    ent = "encoder.encoder.layer.0.output.dense.bias"
+    w4 = dict(w)
+    w4[ent] = np.zeros(1024, np.int64)  # 8-byte elements; the header below says I64
+    _write_safetensors(p, w4)
+    raw = p.read_bytes()
+    n = struct.unpack("<Q", raw[:8])[0]
+    hdr = _json.loads(raw[8:8 + n])
+    hdr[ent]["dtype"] = "I64"
+    new_raw = _json.dumps(hdr).encode()
+    p.write_bytes(struct.pack("<Q", len(new_raw)) + new_raw + raw[8 + n:])
+    st, msg = _load_status(p)
+    assert st == 2 and "I64" in msg, (st, msg)
+    # an unknown dtype name -> I/O (format) error
+    hdr[ent]["dtype"] = "Q7"
+    new_raw = _json.dumps(hdr).encode()
+    p.write_bytes(struct.pack("<Q", len(new_raw)) + new_raw + raw[8 + n:])
+    assert _load_status(p)[0] == 6
+
     p = tmp_path / "garbage.safetensors"
     p.write_bytes(b"\x10\x00\x00\x00\x00\x00\x00\x00{not json at all")
     assert _load_status(p)[0] == 6
