@@ -134,3 +134,28 @@ def test_raw_text_serving_matches_oracle(weights_file, tmp_path):
         for p, t, (pr, _) in zip(r.predictions, e.tasks, dec):
             np.testing.assert_allclose(p.probabilities, pr[:len(t.labels)], atol=PROB_ATOL, rtol=0)
     model.close()
+
+
+def test_stream_serving_sharded_over_two_handles_matches_one(weights_file):
+    """The serving loop's stream path with each chunk's rows split over two model handles
+    (gdc_classify_sharded; both on device 0 here) gives the same predictions as one handle."""
+    import gliner_decide_metal_b200 as g
+    from gliner_decide_metal_b200 import serve, synthetic
+    layers, vocab = 2, 128011
+    path, _ = weights_file(11, layers, vocab)
+    cfg = g.DeBERTaV2Configuration(num_hidden_layers=layers, vocab_size=vocab)
+    models = [g.GLiNERDecideClassifier(path, configuration=cfg, device=0) for _ in range(2)]
+    ex = []
+    for i, (ids, markers, n_labels, ml) in enumerate(synthetic.mixed_rows(40, seed=31)):
+        tasks = [g.DecisionTask(f"t{h}", tuple(f"l{j}" for j in range(n)), m) for h, (n, m) in
+                 enumerate(zip(n_labels, ml))]
+        ex.append(serve.TokenizedExample(f"r{i}", [int(x) for x in ids], tasks, [list(p) for p in markers]))
+    one = serve.run_examples(models[0], ex, batch_size=16, group_by="stream")
+    two = serve.run_examples(models, ex, batch_size=16, group_by="stream")
+    for a, b in zip(one, two):
+        assert a.id == b.id
+        for pa, pb in zip(a.predictions, b.predictions):
+            assert pa.labels == pb.labels
+            np.testing.assert_allclose(pa.probabilities, pb.probabilities, rtol=0, atol=1e-6)
+    for m in models:
+        m.close()
