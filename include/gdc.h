@@ -154,7 +154,9 @@ gdc_status gdc_classify(gdc_model* model, const gdc_input* input, int collect_pr
  * marker_indices int32, marker_mask float32; logits float32 device buffer (and
  * optional fp16). Enqueues on `stream` (a cudaStream_t, NULL = the model's stream)
  * and returns without synchronising. Inputs are checked on the device: an
- * out-of-range id or marker index sets a flag reported by gdc_check_errors(). */
+ * out-of-range id or marker index sets a flag reported by gdc_check_errors().
+ * All calls on one model share its device workspace: calls enqueued on different
+ * streams must be ordered by the caller (the internal mutex only orders the host side). */
 gdc_status gdc_classify_device(gdc_model* model, int32_t batch, int32_t seq_len,
                                int32_t max_heads, int32_t max_options,
                                const int32_t* d_input_ids, const uint16_t* d_attention_mask,
