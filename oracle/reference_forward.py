@@ -367,7 +367,8 @@ def decode(logits_row: np.ndarray, n_labels, multi_label):
     for t, (n, ml) in enumerate(zip(n_labels, multi_label)):
         x = np.asarray(logits_row[t, :n], dtype=np.float64)
         if ml:
-            p = 1.0 / (1.0 + np.exp(-x))
+            with np.errstate(over="ignore"):  # exp(10000) = inf gives p = 0, as Double does
+                p = 1.0 / (1.0 + np.exp(-x))
             sel = [i for i in range(n) if p[i] >= 0.5]
             if not sel:
                 sel = [int(np.argmax(p))]

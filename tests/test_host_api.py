@@ -244,3 +244,24 @@ def test_packed_row_layout_rule():
     ext, off = g.packed_row_layout(mask, mk, mm)
     assert list(ext) == [7, 6, 8, 8]
     assert list(off) == [0, 7, 13, 21, 29]
+
+
+def test_decode_edge_cases_match_oracle():
+    """Decode edges (RawCLI.swift:182-223): exact ties pick the first label, a logit of 0
+    (sigmoid 0.5) is selected, a multi-label task with every sigmoid below 0.5 falls back to
+    its argmax, and -10000 fills and huge magnitudes stay finite."""
+    import gliner_decide_metal_b200 as g
+    cases = [
+        ([1.0, 1.0, 0.5], False), ([2.0, 3.0, 3.0, 1.0], False), ([0.0, -1.0], True),
+        ([-3.0, -2.0, -2.0], True), ([-10000.0, -10000.0, -10000.0], False), ([-10000.0, -10000.0], True),
+        ([80.0, -80.0, 0.0], False), ([1e4, -1e4], True), ([0.0, 0.0, 0.0, 0.0], False), ([0.0, 0.0], True),
+    ]
+    O = max(len(c) for c, _ in cases)
+    for vals, multi in cases:
+        logits = np.full((1, 1, O), -10000.0, np.float32)
+        logits[0, 0, :len(vals)] = vals
+        probs, sel = g.decode_batch(logits, np.array([[len(vals)]], np.int32), np.array([[int(multi)]], np.uint8))
+        (p, s), = rf.decode(logits[0][[0]], [len(vals)], [multi])
+        np.testing.assert_allclose(probs[0, 0, :len(vals)], p, rtol=0, atol=1e-12)
+        assert np.flatnonzero(sel[0, 0, :len(vals)]).tolist() == s, (vals, multi)
+        assert np.isfinite(probs).all()
