@@ -15,9 +15,10 @@
 // epilogue of one tile overlaps the main loop of the next. All waits are bounded.
 //
 // Tail split: the tiles are 256 x BN; when the last wave over the CTA pairs would be at most
-// half full, its tiles are split into two 256 x BN/2 tiles each, so that wave takes half the
-// time. The row count may come from device memory (packed encoder rows), so the split is
-// decided in the kernel; every role derives the same tile list from (M, N, pairs).
+// half (a quarter) full, its tiles are split into two (four) 256 x BN/2 (BN/4) tiles each, so
+// that wave runs narrower tiles on more pairs. The row count may come from device memory
+// (packed encoder rows), so the split is decided in the kernel; every role derives the same
+// tile list from (M, N, pairs).
 #include <cuda.h>
 
 #include "kernels.h"
@@ -65,29 +66,40 @@ struct PairTile {
 };
 
 // Tile t of the launch's list: full-width tiles in M-fastest order, then (when the tail is
-// split) the halves of the last `rem` full-width tiles.
+// split) the `sp` parts of each of the last `rem` full-width tiles.
 struct PairTiles {
-  int num_m, n_main, rem, num_tiles, bn;
-  __device__ PairTiles(int M, int N, int BN, int pairs, bool can_split) : bn(BN) {
+  int num_m, n_main, rem, sp, num_tiles, bn;
+  // max_split: the widest split the tile width allows (the parts' columns per epilogue
+  // warp stay whole 32-column chunks: BN / (2 sp) % 32 == 0)
+  __device__ PairTiles(int M, int N, int BN, int pairs, int max_split) : bn(BN) {
     num_m = (M + 255) / 256;
     const int num_big = num_m * (N / BN);
     rem = pairs > 0 ? num_big % pairs : 0;
-    if (!can_split || rem == 0 || 2 * rem > pairs) rem = 0;
+    sp = 1;
+    if (rem > 0)
+      for (int f = max_split; f >= 2; f >>= 1)
+        if (f * rem <= pairs) {
+          sp = f;
+          break;
+        }
+    if (sp == 1) rem = 0;
     n_main = num_big - rem;
-    num_tiles = n_main + 2 * rem;
+    num_tiles = n_main + sp * rem;
   }
   __device__ PairTile operator()(int t) const {
     if (t < n_main) return PairTile{t % num_m, (t / num_m) * bn, bn};
     const int u = t - n_main;
-    const int big = n_main + (u >> 1);
-    return PairTile{big % num_m, (big / num_m) * bn + (u & 1) * (bn / 2), bn / 2};
+    const int big = n_main + u / sp;
+    const int w = bn / sp;
+    return PairTile{big % num_m, (big / num_m) * bn + (u % sp) * w, w};
   }
 };
 
 template <int BN, int ACT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                     const __grid_constant__ CUtensorMap tm_w_half, const __grid_constant__ CUtensorMap tm_out,
+                     const __grid_constant__ CUtensorMap tm_w_half, const __grid_constant__ CUtensorMap tm_w_quarter,
+                     const __grid_constant__ CUtensorMap tm_out,
                      const __half* __restrict__ bias, int M_cap, int N, int K, int* err,
                      const int32_t* __restrict__ m_dev) {
   using S = PairShape<BN>;
@@ -111,8 +123,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int kblocks = (K + kBK - 1) / kBK;  // a last half block reads TMA zero fill
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
-  // halves of BN = 256 / 128 keep the epilogue's 32-column chunks whole
-  const PairTiles tiles(M, N, BN, num_pairs, BN % 128 == 0);
+  // parts of BN keep the epilogue's 32-column chunks whole: BN = 256 splits in 2 or 4,
+  // BN = 128 in 2, BN = 192 not at all
+  const PairTiles tiles(M, N, BN, num_pairs, BN % 256 == 0 ? 4 : (BN % 128 == 0 ? 2 : 1));
   const int num_tiles = tiles.num_tiles;
 
   if (threadIdx.x == 0) {
@@ -142,13 +155,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       ptx::prefetch_tensor_map(&tm_a);
       ptx::prefetch_tensor_map(&tm_w);
       ptx::prefetch_tensor_map(&tm_w_half);
+      ptx::prefetch_tensor_map(&tm_w_quarter);
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
         const PairTile ti = tiles(tile);
-        const bool full_w = ti.bn == BN;
+        const CUtensorMap* tw = ti.bn == BN ? &tm_w : (ti.bn == BN / 2 ? &tm_w_half : &tm_w_quarter);
         const int w_rows = ti.bn / 2;  // rows of W this CTA loads
         const uint32_t tx = 2u * uint32_t(S::kABytes + 2 * w_rows * kAtomK * 2);
         for (int kb = 0; kb < kblocks; ++kb) {
@@ -162,8 +176,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int h = 0; h < 2; ++h) {
             ptx::tma_load_2d_pair(s_a + stage * S::kABytes + h * S::kAHalf, &tm_a, kb * kBK + h * kAtomK,
                                   ti.mb * 256 + int(rank) * 128, leader_full);
-            ptx::tma_load_2d_pair(s_b + stage * S::kBBytes + h * S::kBHalf, full_w ? &tm_w : &tm_w_half,
-                                  kb * kBK + h * kAtomK, ti.n0 + int(rank) * w_rows, leader_full);
+            ptx::tma_load_2d_pair(s_b + stage * S::kBBytes + h * S::kBHalf, tw, kb * kBK + h * kAtomK,
+                                  ti.n0 + int(rank) * w_rows, leader_full);
           }
           ++issued;
           if (++stage == S::kStages) {
@@ -191,6 +205,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0 && leader) {
       constexpr uint32_t idesc_full = ptx::idesc_f16_f32(256, BN);
       constexpr uint32_t idesc_half = ptx::idesc_f16_f32(256, BN / 2);
+      constexpr uint32_t idesc_quarter = ptx::idesc_f16_f32(256, BN / 4);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -204,7 +219,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-        const uint32_t idesc = tiles(tile).bn == BN ? idesc_full : idesc_half;
+        const int tbn = tiles(tile).bn;
+        const uint32_t idesc = tbn == BN ? idesc_full : (tbn == BN / 2 ? idesc_half : idesc_quarter);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!ptx::mbar_wait(&full[stage], phase, err)) {
             ok = false;
@@ -314,8 +330,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 template <int BN, int ACT>
 gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& twh,
-                               const CUtensorMap& to, const __half* bias, int M, int N, int K, cudaStream_t stream,
-                               int* err, const int32_t* m_dev) {
+                               const CUtensorMap& twq, const CUtensorMap& to, const __half* bias, int M, int N, int K,
+                               cudaStream_t stream, int* err, const int32_t* m_dev) {
   using S = PairShape<BN>;
   auto kern = gemm_pair_kernel<BN, ACT>;
   static bool configured[64] = {};
@@ -329,7 +345,7 @@ gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, con
   const int num_tiles = ((M + 255) / 256) * (N / BN);
   const int pairs_avail = device_sm_count(dev) / 2;
   const int pairs = num_tiles < pairs_avail ? num_tiles : pairs_avail;
-  kern<<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(ta, tw, twh, to, bias, M, N, K, err, m_dev);
+  kern<<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(ta, tw, twh, twq, to, bias, M, N, K, err, m_dev);
   return check_launch("gemm_pair_kernel");
 }
 
@@ -362,17 +378,18 @@ gdc_status launch_linear_pair(const __half* a, int64_t lda, const __half* w, con
   // tiles are then the best start wherever N allows them.
   const int bn = (m_dev != nullptr && N % 256 == 0) ? 256 : choose_bn(M, N, device_sm_count(dev) / 2);
   if (bn == 0) return set_error(GDC_ERR_UNSUPPORTED, "linear: N=%d is not a multiple of 128", N);
-  CUtensorMap ta, tw, twh, to;
+  CUtensorMap ta, tw, twh, twq, to;
   GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), 128));
   GDC_TRY(make_tmap_2d(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 2)));
   GDC_TRY(make_tmap_2d(&twh, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 4)));
+  GDC_TRY(make_tmap_2d(&twq, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 8 > 0 ? bn / 8 : 1)));
   GDC_TRY(make_tmap_2d_out32(&to, out, uint64_t(M), uint64_t(N), uint64_t(ldo)));
   const int m = int(M);
 #define GDC_PAIR_CASE(BNV)                                                                              \
   if (bn == BNV) {                                                                                      \
-    if (act == kActGelu) return launch_pair_variant<BNV, kActGelu>(ta, tw, twh, to, bias, m, N, K, stream, err, m_dev); \
-    if (act == kActRelu) return launch_pair_variant<BNV, kActRelu>(ta, tw, twh, to, bias, m, N, K, stream, err, m_dev); \
-    return launch_pair_variant<BNV, kActNone>(ta, tw, twh, to, bias, m, N, K, stream, err, m_dev); \
+    if (act == kActGelu) return launch_pair_variant<BNV, kActGelu>(ta, tw, twh, twq, to, bias, m, N, K, stream, err, m_dev); \
+    if (act == kActRelu) return launch_pair_variant<BNV, kActRelu>(ta, tw, twh, twq, to, bias, m, N, K, stream, err, m_dev); \
+    return launch_pair_variant<BNV, kActNone>(ta, tw, twh, twq, to, bias, m, N, K, stream, err, m_dev); \
   }
   GDC_PAIR_CASE(256)
   GDC_PAIR_CASE(192)
