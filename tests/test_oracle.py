@@ -123,3 +123,39 @@ def test_decode_rules():
     assert s1 == [1]  # all sigmoids < 0.5: first argmax among the 3 labels (tie -> first)
     (p2, s2), = rf.decode(np.array([[0.1, -0.2, 3.0]]), [3], [True])
     assert s2 == [0, 2]
+
+
+def test_padding_past_the_extent_does_not_change_logits():
+    """The premise of packed encoder rows, checked on the oracle: a row's logits are the same
+    whether it is padded to its bucket or cut at its extent (last valid position or active
+    marker + 1), because padded positions only ever act as masked keys (weight exactly 0).
+    fp64, no fp16 rounding: a padded position that leaked would move the logits by far more
+    than the 1e-6 allowed, which only covers BLAS summing a shorter row in another order."""
+    from gliner_decide_metal_b200 import synthetic
+    layers, vocab = 2, 500
+    w = synthetic.make_weights(seed=3, num_layers=layers, vocab=vocab)
+    W = rf.OracleWeights(w, rf.OracleConfig(num_hidden_layers=layers, vocab_size=vocab))
+    rng = np.random.default_rng(8)
+    L = 96
+    for case in range(4):
+        n = int(rng.integers(5, 60))
+        ids = rng.integers(3, vocab, (1, L))
+        ids[0, n:] = 0
+        mask = np.zeros((1, L), np.float16)
+        mask[0, :n] = 1
+        if case == 3:
+            mask[0, 2:4] = 0  # a hole inside the valid span
+        mk = rng.integers(0, n, (1, 2, 3))
+        mm = np.ones((1, 2, 3), np.float32)
+        mm[0, 1, 2] = 0
+        if case == 2:
+            mk[0, 1, 1] = n + 7  # an active marker in the padding extends the extent
+        ext = max(n, int(mk[mm > 0].max()) + 1)
+        full = rf.forward(W, ids, mask, mk, mm, fp16_rounding=False, dtype=np.float64)
+        cut = rf.forward(W, ids[:, :ext], mask[:, :ext], mk, mm, fp16_rounding=False, dtype=np.float64)
+        np.testing.assert_allclose(cut, full, rtol=0, atol=1e-6)
+        if case == 0:
+            # control: dropping the last valid position does change the logits
+            short = rf.forward(W, ids[:, :n - 1], mask[:, :n - 1], np.minimum(mk, n - 2), mm,
+                               fp16_rounding=False, dtype=np.float64)
+            assert np.abs(short - full)[mm > 0].max() > 1e-4
