@@ -172,6 +172,9 @@ def _pre_tokenizer(spec: Optional[dict]):
             return pieces
         return seq
     if kind == "Metaspace":
+        # prepend_scheme "first" is applied like "always" (one call sees one text); the
+        # tokenizers library also skips the prefix when a normalizer removed leading text,
+        # which DeBERTa-v3's "always" never does
         rep = spec.get("replacement", "▁")
         scheme = spec.get("prepend_scheme", "always" if spec.get("add_prefix_space", True) else "never")
         split = spec.get("split", True)

@@ -241,3 +241,30 @@ def test_raw_stream_pipeline_matches_shape_grouping(tok_dir):
     for x, y in zip(a, b):
         assert [(p.task, p.labels, p.probabilities) for p in x.predictions] == \
             [(p.task, p.labels, p.probabilities) for p in y.predictions]
+
+
+@pytest.mark.parametrize("variant", ["lower_punct", "prepend_never", "whitespace", "nfd"])
+def test_pipeline_variants_match_tokenizers_library(tmp_path, variant):
+    """Other normalizer / pre-tokenizer chains a tokenizer.json may carry (Lowercase,
+    Punctuation, WhitespaceSplit, NFD, Metaspace prepend schemes) against the library."""
+    from tokenizers import Regex, normalizers, pre_tokenizers
+    from gliner_decide_metal_b200.tokenizer import UnigramTokenizer
+    tok = _synthetic(seed=5, n_pieces=500)
+    if variant == "lower_punct":
+        tok.normalizer = normalizers.Sequence([normalizers.Lowercase(), normalizers.Strip()])
+        tok.pre_tokenizer = pre_tokenizers.Sequence([pre_tokenizers.Punctuation(behavior="isolated"),
+                                                     pre_tokenizers.Metaspace(replacement="▁", prepend_scheme="always")])
+    elif variant == "prepend_never":
+        tok.pre_tokenizer = pre_tokenizers.Metaspace(replacement="▁", prepend_scheme="never")
+    elif variant == "whitespace":
+        tok.normalizer = normalizers.Replace(Regex("[0-9]"), "")
+        tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    elif variant == "nfd":
+        tok.normalizer = normalizers.NFD()
+    tok.save(str(tmp_path / "tokenizer.json"))
+    mine = UnigramTokenizer.from_file(tmp_path / "tokenizer.json")
+    rng = np.random.default_rng(11)
+    texts = ["Hello, World!", "x", "a.b,c", "  spaced   out  ", "Café über"]
+    texts += [_random_text(rng, int(rng.integers(1, 30))) for _ in range(200)]
+    for t in texts:
+        assert mine.encode(t) == tok.encode(t, add_special_tokens=False).ids, (variant, t)
