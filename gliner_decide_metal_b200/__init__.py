@@ -15,8 +15,9 @@ shantanugoel/gliner-decide-metal) over the C ABI in ``include/gdc.h``:
 * errors                                WeightStoreError (Weights.swift:4-19), NativeTokenizerError
                                         (NativeTokenizer.swift:5-23)
 
-All compute runs in ``libgdc.so`` on the GPU; importing fails loudly if the library
-is missing.
+All compute runs in ``libgdc.so`` on the GPU. The library is mapped by the first call
+that needs it (model load, classify, layout, decode); that call raises ImportError if
+the library is missing. There is no CPU fallback.
 """
 from __future__ import annotations
 

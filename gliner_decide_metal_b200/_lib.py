@@ -1,7 +1,10 @@
 """ctypes binding of ``libgdc.so`` (declarations in ``include/gdc.h``).
 
 The library is built in-tree by ``gliner_decide_metal_b200.build``. There is no
-fallback: if the shared library is missing or fails to load, importing the API raises.
+fallback: if the shared library is missing or fails to load, the first call through
+``lib`` raises ImportError. The library is mapped on that first call, not at import, so
+that host-only users of the package (the synthetic-data generators, the safetensors
+reader) do not load it.
 """
 from __future__ import annotations
 
@@ -87,6 +90,7 @@ SIGNATURES = [
 
 
 def load():
+    """Maps libgdc.so and sets the ctypes signature of every function in include/gdc.h."""
     if not LIB_PATH.exists():
         raise ImportError(
             f"{LIB_PATH} is missing: build it with `python gliner_decide_metal_b200/build.py` "
@@ -99,4 +103,27 @@ def load():
     return lib
 
 
-lib = load()
+class _LazyLibrary:
+    """Attribute access loads libgdc.so once (thread-safe) and forwards to it."""
+
+    def __init__(self):
+        import threading
+        self._lock = threading.Lock()
+        self._cdll = None
+
+    def _get(self):
+        if self._cdll is None:
+            with self._lock:
+                if self._cdll is None:
+                    self._cdll = load()
+        return self._cdll
+
+    @property
+    def loaded(self) -> bool:
+        return self._cdll is not None
+
+    def __getattr__(self, name):
+        return getattr(self._get(), name)
+
+
+lib = _LazyLibrary()

@@ -281,8 +281,16 @@ gdc_status gdc_classify_device(gdc_model* m, int32_t B, int32_t L, int32_t Hm, i
   std::lock_guard<std::mutex> lk(m->mu);
   GDC_CUDA_TRY(cudaSetDevice(m->device));
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
-  return forward(m, B, L, Hm, O, ids, reinterpret_cast<const __half*>(mask), markers, marker_mask, logits,
-                 reinterpret_cast<__half*>(logits16), s, false);
+  GDC_TRY(forward(m, B, L, Hm, O, ids, reinterpret_cast<const __half*>(mask), markers, marker_mask, logits,
+                  reinterpret_cast<__half*>(logits16), s, false));
+  if (s != m->stream) {
+    // order the model's stream after this forward, so gdc_check_errors (which synchronises
+    // the model's stream) reads the error word only once this forward has finished with it
+    if (m->call_done == nullptr) GDC_CUDA_TRY(cudaEventCreateWithFlags(&m->call_done, cudaEventDisableTiming));
+    GDC_CUDA_TRY(cudaEventRecord(m->call_done, s));
+    GDC_CUDA_TRY(cudaStreamWaitEvent(m->stream, m->call_done, 0));
+  }
+  return GDC_OK;
 }
 
 gdc_status gdc_check_errors(gdc_model* m) {

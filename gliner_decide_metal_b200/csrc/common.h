@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include <cuda_runtime.h>
@@ -38,6 +39,20 @@ inline gdc_status check_launch(const char* what) {
   if (e != cudaSuccess)
     return set_error(GDC_ERR_CUDA, "kernel launch %s failed: %s", what, cudaGetErrorString(e));
   return GDC_OK;
+}
+
+// Runs `init` once per device ordinal (0..63) over all host threads and returns its result
+// on every later call. Kernel attributes and device queries are set up this way because
+// distinct model handles on one device may reach a kernel's first launch concurrently.
+struct PerDeviceOnce {
+  std::once_flag flag[64];
+  int result[64] = {};
+};
+
+template <typename F>
+int per_device_once(PerDeviceOnce& once, int dev, F&& init) {
+  std::call_once(once.flag[dev], [&] { once.result[dev] = int(init()); });
+  return once.result[dev];
 }
 
 // Device error flag bits written by kernels (bounded waits, input checks).

@@ -40,15 +40,15 @@ gdc_status launch_attention(const __half* qkv, const __half* pos_qk, const __hal
   GDC_TRY(make_tmap_2d(&tm_qkv, qkv, uint64_t(batch) * uint64_t(seq_len), uint64_t(3 * E), uint64_t(3 * E),
                        attn::kTile));
   GDC_TRY(make_tmap_2d(&tm_pos, pos_qk, 512, uint64_t(2 * E), uint64_t(2 * E), attn::kWin));
-  static bool configured[64] = {};
+  static PerDeviceOnce configured;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attn::attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         attn::kSmemBytes);
-    if (e != cudaSuccess) return set_error(GDC_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
-    configured[dev] = true;
-  }
+  if (dev < 0 || dev >= 64) return set_error(GDC_ERR_CUDA, "device ordinal out of range");
+  const cudaError_t ce = cudaError_t(per_device_once(configured, dev, [] {
+    return cudaFuncSetAttribute(attn::attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                attn::kSmemBytes);
+  }));
+  if (ce != cudaSuccess) return set_error(GDC_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(ce));
   const long long items = (long long)((seq_len + attn::kTile - 1) / attn::kTile) * heads * batch;
   if (items > (1ll << 30)) return set_error(GDC_ERR_UNSUPPORTED, "attention: too many work items");
   const int sms = device_sm_count(dev);

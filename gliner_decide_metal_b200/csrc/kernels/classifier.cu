@@ -65,7 +65,10 @@ __global__ void classifier_out_kernel(const __half* __restrict__ h, const __half
   }
 }
 
-// One thread per (row, task).
+// One thread per (row, task). RawCLI.swift:182-223 decodes in Swift Double, so the
+// arithmetic here is float64 as well (probabilities are stored as float32): the
+// selections then equal the host decode's, including first-argmax ties and logits whose
+// sigmoid or shifted exponential underflows to 0.
 __global__ void decode_kernel(const float* __restrict__ logits, int batch, int max_heads, int max_options,
                               const int32_t* __restrict__ n_labels, const uint8_t* __restrict__ multi_label,
                               float* __restrict__ probs, uint8_t* __restrict__ selected) {
@@ -82,29 +85,38 @@ __global__ void decode_kernel(const float* __restrict__ logits, int batch, int m
   }
   if (n <= 0) return;
   if (multi_label[t]) {
+    // unshifted sigmoid; select p >= 0.5, else the first argmax
     int best = 0;
+    double best_p = -1.0;
     bool any = false;
     for (int o = 0; o < n; ++o) {
-      p[o] = 1.0f / (1.0f + expf(-x[o]));
-      if (p[o] >= 0.5f) {
+      const double q = 1.0 / (1.0 + exp(-double(x[o])));
+      p[o] = float(q);
+      if (q >= 0.5) {
         s[o] = 1;
         any = true;
       }
-      if (p[o] > p[best]) best = o;
+      if (q > best_p) {
+        best_p = q;
+        best = o;
+      }
     }
     if (!any) s[best] = 1;
   } else {
-    float m = x[0];
-    for (int o = 1; o < n; ++o) m = fmaxf(m, x[o]);
-    float sum = 0.f;
-    for (int o = 0; o < n; ++o) {
-      p[o] = expf(x[o] - m);
-      sum += p[o];
-    }
+    // max-subtracted softmax, first argmax
+    double m = double(x[0]);
+    for (int o = 1; o < n; ++o) m = fmax(m, double(x[o]));
+    double sum = 0.0;
+    for (int o = 0; o < n; ++o) sum += exp(double(x[o]) - m);
     int best = 0;
+    double best_p = -1.0;
     for (int o = 0; o < n; ++o) {
-      p[o] /= sum;
-      if (p[o] > p[best]) best = o;
+      const double q = exp(double(x[o]) - m) / sum;
+      p[o] = float(q);
+      if (q > best_p) {
+        best_p = q;
+        best = o;
+      }
     }
     s[best] = 1;
   }

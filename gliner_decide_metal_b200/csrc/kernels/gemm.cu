@@ -270,14 +270,14 @@ gdc_status launch_gemm_variant(const CUtensorMap& ta, const CUtensorMap& tw, con
                                const int32_t* m_dev) {
   using S = GemmShape<BN>;
   auto kern = gemm_tn_kernel<BN, ACT>;
-  static bool configured[64] = {};
+  static PerDeviceOnce configured;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return set_error(GDC_ERR_CUDA, "device ordinal out of range");
-  if (!configured[dev]) {
-    GDC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes));
-    configured[dev] = true;
-  }
+  const cudaError_t ce = cudaError_t(per_device_once(configured, dev, [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
+  }));
+  if (ce != cudaSuccess) return set_error(GDC_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(ce));
   const int num_tiles = ((M + kBM - 1) / kBM) * (N / BN);
   const int grid = num_tiles < device_sm_count(dev) ? num_tiles : device_sm_count(dev);
   kern<<<grid, kThreads, S::kSmemBytes, stream>>>(ta, tw, bias, out, M, N, K, ldo, err, m_dev);
@@ -333,14 +333,13 @@ gdc_status make_tmap_2d_out32(void* map_out, const __half* base, uint64_t rows, 
 }
 
 int device_sm_count(int device) {
-  static int counts[64] = {};
+  static PerDeviceOnce counts;
   if (device < 0 || device >= 64) return 148;
-  if (counts[device] == 0) {
+  return per_device_once(counts, device, [&] {
     int c = 0;
     if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || c <= 0) c = 148;
-    counts[device] = c;
-  }
-  return counts[device];
+    return c;
+  });
 }
 
 gdc_status launch_linear(const __half* a, int64_t lda, const __half* w, const __half* bias, __half* out,

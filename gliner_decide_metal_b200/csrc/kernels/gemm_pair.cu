@@ -334,14 +334,14 @@ gdc_status launch_pair_variant(const CUtensorMap& ta, const CUtensorMap& tw, con
                                cudaStream_t stream, int* err, const int32_t* m_dev) {
   using S = PairShape<BN>;
   auto kern = gemm_pair_kernel<BN, ACT>;
-  static bool configured[64] = {};
+  static PerDeviceOnce configured;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return set_error(GDC_ERR_CUDA, "device ordinal out of range");
-  if (!configured[dev]) {
-    GDC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes));
-    configured[dev] = true;
-  }
+  const cudaError_t ce = cudaError_t(per_device_once(configured, dev, [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
+  }));
+  if (ce != cudaSuccess) return set_error(GDC_ERR_CUDA, "pair gemm smem attribute: %s", cudaGetErrorString(ce));
   const int num_tiles = ((M + 255) / 256) * (N / BN);
   const int pairs_avail = device_sm_count(dev) / 2;
   const int pairs = num_tiles < pairs_avail ? num_tiles : pairs_avail;

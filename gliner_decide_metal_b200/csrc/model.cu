@@ -277,8 +277,8 @@ void model_free(gdc_model* m) {
   if (w.h_in) cudaFreeHost(w.h_in);
   if (w.h_out) cudaFreeHost(w.h_out);
   for (auto e : m->events) cudaEventDestroy(e);
-  for (auto& g : m->graphs)
-    if (g.exec) cudaGraphExecDestroy(g.exec);
+  if (m->call_done) cudaEventDestroy(m->call_done);
+  for (auto& g : m->graphs) release_graph(g);
   if (m->weight_pool) cudaFree(m->weight_pool);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
@@ -342,28 +342,36 @@ gdc_status ensure_workspace(gdc_model* m, int64_t tokens, int64_t markers) {
 
 namespace {
 
-// Records an event after the kernels of `cls` when profiling.
+// Records an event after the kernels of `cls` when profiling: on the stream (eager
+// forwards, m->events), or as an event node of the graph being captured (graph->events).
 struct StageRecorder {
   gdc_model* m;
   cudaStream_t s;
   bool on;
   bool named;
-  void begin() {
-    if (!on) return;
-    if (m->events_used < m->events.size()) {
-      cudaEventRecord(m->events[m->events_used], s);
-      m->event_class[m->events_used] = -1;
-      ++m->events_used;
+  ForwardGraph* graph = nullptr;
+  void record(int cls) {
+    if (graph != nullptr) {
+      if (graph->events_used < graph->events.size()) {
+        cudaEventRecordWithFlags(graph->events[graph->events_used], s, cudaEventRecordExternal);
+        graph->event_class[graph->events_used] = cls;
+        ++graph->events_used;
+      }
+      return;
     }
-  }
-  void end(int cls, const std::string& name) {
-    if (!on) return;
     if (m->events_used < m->events.size()) {
       cudaEventRecord(m->events[m->events_used], s);
       m->event_class[m->events_used] = cls;
       ++m->events_used;
-      if (named) m->stage_names.push_back(name);
     }
+  }
+  void begin() {
+    if (on) record(-1);
+  }
+  void end(int cls, const std::string& name) {
+    if (!on) return;
+    record(cls);
+    if (named && graph == nullptr) m->stage_names.push_back(name);
   }
 };
 
@@ -439,31 +447,46 @@ bool graphs_enabled() {
 
 // The graph slot of a shape (created on first use; the least recently used slot is
 // recycled beyond 8 shapes).
-ForwardGraph& graph_slot(gdc_model* m, int B, int L, int Hm, int O, bool packed) {
+ForwardGraph& graph_slot(gdc_model* m, int B, int L, int Hm, int O, bool packed, bool profiled) {
   for (auto& g : m->graphs)
-    if (g.batch == B && g.seq_len == L && g.max_heads == Hm && g.max_options == O && g.packed == packed) return g;
+    if (g.batch == B && g.seq_len == L && g.max_heads == Hm && g.max_options == O && g.packed == packed &&
+        g.profiled == profiled)
+      return g;
+  ForwardGraph* slot = nullptr;
   if (m->graphs.size() >= 8) {
     auto it = std::min_element(m->graphs.begin(), m->graphs.end(),
                                [](const ForwardGraph& x, const ForwardGraph& y) { return x.last_use < y.last_use; });
-    if (it->exec) cudaGraphExecDestroy(it->exec);
-    *it = ForwardGraph{};
-    it->batch = B, it->seq_len = L, it->max_heads = Hm, it->max_options = O, it->packed = packed;
-    return *it;
+    release_graph(*it);
+    slot = &*it;
+  } else {
+    m->graphs.emplace_back();
+    slot = &m->graphs.back();
   }
-  ForwardGraph g;
-  g.batch = B, g.seq_len = L, g.max_heads = Hm, g.max_options = O, g.packed = packed;
-  m->graphs.push_back(g);
-  return m->graphs.back();
+  slot->batch = B, slot->seq_len = L, slot->max_heads = Hm, slot->max_options = O, slot->packed = packed;
+  slot->profiled = profiled;
+  return *slot;
 }
 
-// Captures the forward of `g`'s shape on the workspace staging buffers.
+// Captures the forward of `g`'s shape on the workspace staging buffers (with one event node
+// after every kernel group when g.profiled).
 gdc_status capture_graph(gdc_model* m, ForwardGraph& g, cudaStream_t s) {
   Workspace& w = m->ws;
   if (g.exec) {
     cudaGraphExecDestroy(g.exec);
     g.exec = nullptr;
   }
-  StageRecorder off{m, s, false, false};
+  StageRecorder off{m, s, g.profiled, false};
+  if (g.profiled) {
+    const size_t need = size_t(7 * m->layers_n + 4);
+    while (g.events.size() < need) {
+      cudaEvent_t e;
+      GDC_CUDA_TRY(cudaEventCreate(&e));
+      g.events.push_back(e);
+      g.event_class.push_back(-1);
+    }
+    g.events_used = 0;
+    off.graph = &g;
+  }
   GDC_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   const gdc_status st = enqueue_forward(m, g.batch, g.seq_len, g.max_heads, g.max_options, w.ids, w.mask,
                                         w.marker_idx, w.marker_mask, w.logits, w.logits16, s, off, g.packed);
@@ -501,7 +524,7 @@ gdc_status forward(gdc_model* m, int B, int L, int Hm, int O, const int32_t* ids
   GDC_TRY(ensure_workspace(m, T, R));
   Workspace& w = m->ws;
   StageRecorder rec{m, s, m->profiling || named_stages, named_stages};
-  if (rec.on) {
+  if (rec.on && (named_stages || !graphs_enabled())) {
     // one event after every kernel group; make sure the pool is large enough
     const size_t need = m->events_used + size_t(7 * m->layers_n + 4);
     while (m->events.size() < need) {
@@ -518,7 +541,20 @@ gdc_status forward(gdc_model* m, int B, int L, int Hm, int O, const int32_t* ids
   // ws.logits16, so caller buffers elsewhere are copied in and out around it. The first
   // call of a shape runs eagerly (one-time kernel attribute set-up happens outside any
   // capture); the second captures the graph.
-  ForwardGraph& g = graph_slot(m, B, L, Hm, O, pack);
+  // With the stage profiler on (rec.on), a separate graph of the shape carries an event node
+  // after every kernel group; each replay is synchronised and its intervals added to the
+  // profiler's totals, so they measure the replayed kernels without eager launch gaps.
+  const bool profiled = rec.on;
+  if (profiled) {
+    const size_t need = m->events_used + size_t(7 * m->layers_n + 4);
+    while (m->events.size() < need) {
+      cudaEvent_t e;
+      GDC_CUDA_TRY(cudaEventCreate(&e));
+      m->events.push_back(e);
+      m->event_class.push_back(-1);
+    }
+  }
+  ForwardGraph& g = graph_slot(m, B, L, Hm, O, pack, profiled);
   g.last_use = ++m->graph_clock;
   if (g.calls++ == 0)
     return enqueue_forward(m, B, L, Hm, O, ids, mask, markers, marker_mask, logits, logits16, s, rec, pack);
@@ -530,15 +566,31 @@ gdc_status forward(gdc_model* m, int B, int L, int Hm, int O, const int32_t* ids
   GDC_CUDA_TRY(cudaGraphLaunch(g.exec, s));
   GDC_TRY(copy_if_needed(logits, w.logits, size_t(R) * 4, s));
   if (logits16) GDC_TRY(copy_if_needed(logits16, w.logits16, size_t(R) * 2, s));
+  if (profiled) {
+    GDC_CUDA_TRY(cudaStreamSynchronize(s));
+    for (size_t e = 1; e < g.events_used; ++e) {
+      const int c = g.event_class[e];
+      if (c < 0) continue;
+      float ms = 0.f;
+      GDC_CUDA_TRY(cudaEventElapsedTime(&ms, g.events[e - 1], g.events[e]));
+      m->prof_ns[c] += double(ms) * 1e6;
+      m->prof_launches[c] += 1;
+    }
+  }
   return GDC_OK;
+}
+
+void release_graph(ForwardGraph& g) {
+  if (g.exec) cudaGraphExecDestroy(g.exec);
+  for (auto e : g.events) cudaEventDestroy(e);
+  g = ForwardGraph{};
 }
 
 void set_row_packing(gdc_model* m, bool on) {
   if (m->pack_rows == on) return;
   m->pack_rows = on;
   if (m->stream) cudaStreamSynchronize(m->stream);
-  for (auto& g : m->graphs)
-    if (g.exec) cudaGraphExecDestroy(g.exec);
+  for (auto& g : m->graphs) release_graph(g);
   m->graphs.clear();
 }
 

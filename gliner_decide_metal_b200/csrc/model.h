@@ -84,11 +84,20 @@ struct Workspace {
 struct ForwardGraph {
   int batch = 0, seq_len = 0, max_heads = 0, max_options = 0;
   bool packed = false;  // row layout the graph was captured with
+  // profiled: the graph also records an event node after every kernel group (the stage
+  // profiler's intervals, measured on the replayed graph instead of eager launches)
+  bool profiled = false;
   int generation = -1;
   int calls = 0;                  // eager calls seen for this shape (captured on the second)
   cudaGraphExec_t exec = nullptr;
   uint64_t last_use = 0;
+  std::vector<cudaEvent_t> events;  // profiled graphs: the event of every node, in order
+  std::vector<int> event_class;     // class of the interval ending at events[i] (-1: none)
+  size_t events_used = 0;
 };
+
+// Destroys a captured forward and its events, leaving an empty slot.
+void release_graph(ForwardGraph& g);
 
 }  // namespace gdc
 
@@ -107,6 +116,7 @@ struct gdc_model {
   bool pack_rows = true;
 
   cudaStream_t stream = nullptr;
+  cudaEvent_t call_done = nullptr;  // end of the last gdc_classify_device on a caller's stream
   std::mutex mu;
 
   void* weight_pool = nullptr;

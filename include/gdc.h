@@ -164,7 +164,10 @@ gdc_status gdc_classify_device(gdc_model* model, int32_t batch, int32_t seq_len,
                                float* d_logits, uint16_t* d_logits_f16, void* stream);
 
 /* Reads and clears the model's device error flags (bounded-wait timeouts,
- * out-of-range ids/markers seen by gdc_classify_device). Synchronises the stream. */
+ * out-of-range ids/markers seen by gdc_classify_device). Waits first for every forward
+ * already enqueued by gdc_classify_device, on the model's stream or on a caller's stream
+ * (each such call ends by making the model's stream wait on the caller's), so the flags of
+ * those calls are complete when they are read. */
 gdc_status gdc_check_errors(gdc_model* model);
 
 /* The model's CUDA stream (cudaStream_t) — for event timing by callers. */
@@ -212,8 +215,10 @@ gdc_status gdc_decode(const float* logits, int32_t batch, int32_t max_heads, int
                       const int32_t* n_labels, const uint8_t* multi_label,
                       double* probabilities, uint8_t* selected);
 
-/* Same decode on the device in float32 (for callers keeping logits in HBM).
- * All pointers are device pointers; enqueued on `stream`. */
+/* Same decode on the device (for callers keeping logits in HBM), RawCLI.swift:182-223:
+ * float64 arithmetic as the reference's Double, probabilities stored as float32,
+ * selections identical to gdc_decode's. All pointers are device pointers; enqueued on
+ * `stream` (NULL = the model's stream). */
 gdc_status gdc_decode_device(gdc_model* model, const float* d_logits, int32_t batch,
                              int32_t max_heads, int32_t max_options, const int32_t* d_n_labels,
                              const uint8_t* d_multi_label, float* d_probabilities,

@@ -63,9 +63,15 @@ def test_golden_parity(name, weights_file):
     W = rf.OracleWeights(w, rf.OracleConfig(num_hidden_layers=layers, vocab_size=vocab))
     ref16 = rf.forward(W, gld["input_ids"], gld["attention_mask"], gld["marker_indices"], gld["marker_mask"])
     np.testing.assert_allclose(got, ref16, atol=LOGIT_ATOL, rtol=0)
-    # probabilities and label sets (single-label softmax over each head's valid options)
+    # probabilities and label sets (single-label softmax over each head's valid options).
+    # The parity target is the reference's own forward, which computes in fp16 between ops;
+    # the fp16-emulating oracle stands for it, and the probabilities must agree with it
+    # within 1e-3. The transformers fixture is an fp32 forward with no fp16 rounding, so
+    # against it the bound is the fp16 rounding of 24 layers (at most 5e-3 on these cases).
     n_labels = (gld["marker_mask"] > 0).sum(-1).astype(np.int32)
     multi = np.zeros_like(n_labels, dtype=np.uint8)
+    pa, pr = _selections_agree(got, ref16.astype(np.float32), n_labels, multi, 1e-3)
+    assert np.abs(pa - pr).max() < PROB_ATOL
     pa, pb = _selections_agree(got, gld["logits"].astype(np.float32), n_labels, multi, 1e-3)
     assert np.abs(pa - pb).max() < 5 * PROB_ATOL
     model.close()
@@ -179,7 +185,8 @@ def test_sharded_equals_single(weights_file):
 def test_full_size_properties(weights_file):
     """BASELINE config 2 (B=32, L=256, 24 layers): rows are independent, so (a) permuting
     rows permutes the logits bit-exactly, (b) a row classified alone equals its row in the
-    batch bit-exactly, (c) two rows match the fp16 oracle within the logit tolerance."""
+    batch bit-exactly, (c) eight rows spread over the batch match the fp16 oracle within the
+    logit tolerance, with probabilities within 1e-3 and the same argmax."""
     import gliner_decide_metal_b200 as g
     from gliner_decide_metal_b200 import synthetic
     c2 = synthetic.config2()
@@ -194,6 +201,11 @@ def test_full_size_properties(weights_file):
                                          c2.marker_mask[5:6])).logits_f32
     assert np.array_equal(one[0], full[5])
     W = rf.OracleWeights(w, rf.OracleConfig())
-    ref = rf.forward(W, c2.input_ids[:2], c2.attention_mask[:2], c2.marker_indices[:2], c2.marker_mask[:2])
-    np.testing.assert_allclose(full[:2], ref, atol=LOGIT_ATOL, rtol=0)
+    rows = [0, 4, 9, 13, 17, 22, 27, 31]
+    ref = rf.forward(W, c2.input_ids[rows], c2.attention_mask[rows], c2.marker_indices[rows], c2.marker_mask[rows])
+    np.testing.assert_allclose(full[rows], ref, atol=LOGIT_ATOL, rtol=0)
+    n_labels = (c2.marker_mask[rows] > 0).sum(-1).astype(np.int32)
+    multi = np.zeros_like(n_labels, dtype=np.uint8)
+    pa, pr = _selections_agree(full[rows], ref.astype(np.float32), n_labels, multi, 1e-3)
+    assert np.abs(pa - pr).max() < PROB_ATOL
     model.close()

@@ -111,3 +111,42 @@ def test_packed_full_model_config2(weights_file):
     ext, off = g.packed_row_layout(c2.attention_mask, c2.marker_indices, c2.marker_mask)
     assert off[-1] < 32 * 256
     model.close()
+
+
+def _tail_split(rows: int, n: int, pairs: int, bn: int = 256, max_split: int = 4) -> int:
+    """The pair GEMM's tail split for a device row count (kernels/gemm_pair.cu, PairTiles):
+    the number of parts each tile of a sparse last wave is cut into (1 = no split)."""
+    num_big = -(-rows // 256) * (n // bn)
+    rem = num_big % pairs
+    f = max_split
+    while rem and f >= 2:
+        if f * rem <= pairs:
+            return f
+        f //= 2
+    return 1
+
+
+def test_packed_equals_dense_through_gemm_tail_splits(weights_file):
+    """Row lengths chosen so the packed batch spans 20 tiles of 256 rows: the out and
+    FFN-down projections (N = 1024) and the QKV projection (N = 3072) then cut their last
+    wave into quarter-width tiles and FFN-up (N = 4096) into half-width tiles, while the
+    dense grid runs full-width tiles only. The logits must still be bit-identical."""
+    import torch
+    import gliner_decide_metal_b200 as g
+    model = _model(weights_file)
+    rng = np.random.default_rng(2024)
+    B, L = 32, 256
+    lengths = np.full(B, 156) + np.concatenate([d := rng.integers(-60, 61, B // 2), -d])
+    inp = _ragged(rng, B, L, 1, 5, 4096, lengths=lengths)
+    ext, off = g.packed_row_layout(inp.attention_mask, inp.marker_indices, inp.marker_mask)
+    rows = int(off[-1])
+    assert 19 * 256 < rows <= 20 * 256
+    pairs = torch.cuda.get_device_properties(0).multi_processor_count // 2
+    assert _tail_split(rows, 1024, pairs) == 4
+    assert _tail_split(rows, 3072, pairs) == 4
+    assert _tail_split(rows, 4096, pairs) == 2
+    assert _tail_split(B * L, 1024, pairs) == 1 and _tail_split(B * L, 4096, pairs) == 1
+    dense, packed = _both(model, inp)
+    assert np.isfinite(dense.astype(np.float32)).all()
+    assert np.array_equal(dense.view(np.uint16), packed.view(np.uint16))
+    model.close()

@@ -27,7 +27,8 @@ def _worker(rank, world, port, mode, out_dir):
     sys.path.insert(0, str(ROOT))
     import torch.distributed as dist
 
-    from gliner_decide_metal_b200.multigpu import max_over_ranks, shard_bounds
+    from bench import max_over_ranks
+    from gliner_decide_metal_b200.multigpu import shard_bounds
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=8))

@@ -34,7 +34,7 @@ def test_noalloc_attention_matches_allocating_entry_point_twice():
     def check(st):
         assert st == 0, lib.gdc_last_error().decode()
 
-    for B, L, seed in [(4, 200, 11), (2, 512, 12)]:
+    for i, (B, L, seed) in enumerate([(4, 200, 11), (2, 512, 12)]):
         qkv, pos, mask = _case(B, L, seed)
         dq, dp, dm = (torch.from_numpy(x).cuda() for x in (qkv, pos, mask))
         ref = torch.full((B * L, E), float("nan"), dtype=torch.float16, device="cuda")
@@ -44,13 +44,17 @@ def test_noalloc_attention_matches_allocating_entry_point_twice():
                                              B, L, H, None))
         torch.cuda.synchronize()
         check(lib.gdc_kernels_check_errors())
+        free_before = torch.cuda.mem_get_info()[0]
         check(lib.gdc_disentangled_attention_noalloc(dq.data_ptr(), dp.data_ptr(), dm.data_ptr(), got.data_ptr(),
                                                      B, L, H, None))
         torch.cuda.synchronize()
-        a = ref.cpu().numpy().astype(np.float32)
-        b = got.cpu().numpy().astype(np.float32)
-        assert np.isfinite(b).all()
-        np.testing.assert_allclose(b, a, rtol=1e-2, atol=4e-3)
+        if i == 0:
+            # the call allocates nothing: device memory the driver reports free did not shrink
+            # (the static array was mapped with the library's module, before the first call)
+            assert torch.cuda.mem_get_info()[0] >= free_before
+        # same kernel, same relative table, same static work split: the fp16 bits agree exactly
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+        assert np.isfinite(got.cpu().numpy().astype(np.float32)).all()
 
 
 def test_noalloc_attention_rejects_sizes_beyond_its_scratch():
