@@ -38,6 +38,8 @@ from dataclasses import dataclass
 from pathlib import Path
 from typing import Dict, List, Optional, Sequence, Tuple
 
+import regex
+
 
 from . import DEFAULT_BUCKETS, DecisionInput, DecisionTask, NoTaskLabelsError, make_input_from_tokens
 
@@ -299,9 +301,33 @@ class UnigramTokenizer:
 
 # --------------------------------------------------------------------------- schema formatter
 
-# NativeTokenizer.swift:70-73 (case-insensitive)
-_WORD_RE = re.compile(r"(?:https?://[^\s]+|www\.[^\s]+)|[a-z0-9._%+-]+@[a-z0-9.-]+\.[a-z]{2,}|@[a-z0-9_]+"
-                      r"|\w+(?:[-_]\w+)*|\S", re.IGNORECASE)
+# NativeTokenizer.swift:67-71: NSRegularExpression (ICU) with .caseInsensitive. The classes
+# are spelled out as ICU defines them, because Python's re module differs on non-ASCII text:
+#   ICU \w = [\p{Alphabetic}\p{Mark}\p{Decimal_Number}\p{Connector_Punctuation}\u200c\u200d]
+#         (re's \w misses combining marks, ZWNJ / ZWJ, Other_Alphabetic symbols such as circled
+#         letters and connector punctuation other than "_", and adds non-decimal numbers such as
+#         superscripts and fractions)
+#   ICU \s = [\t\n\f\r\p{Z}] (re's \s also takes \v, U+001C-U+001F and U+0085)
+#   case-insensitive ASCII letters: simple case folding adds U+017F (long s) to s and U+212A
+#         (Kelvin sign) to k; nothing else folds to an ASCII letter.
+_ICU_W = r"[\p{Alphabetic}\p{Mark}\p{Nd}\p{Pc}\u200c\u200d]"
+_ICU_SPACE = r"\t\n\f\r\p{Z}"
+_LETTERS = r"a-zA-Z\u017f\u212a"
+
+
+def _ci(word: str) -> str:
+    """A literal ASCII word matched case-insensitively, one class per letter."""
+    extra = {"s": "\u017f", "k": "\u212a"}
+    return "".join(f"[{c}{c.upper()}{extra.get(c, '')}]" if c.isalpha() else regex.escape(c) for c in word)
+
+
+_WORD_RE = regex.compile(
+    rf"(?:{_ci('http')}{_ci('s')}?://[^{_ICU_SPACE}]+|{_ci('www.')}[^{_ICU_SPACE}]+)"
+    rf"|[{_LETTERS}0-9._%+-]+@[{_LETTERS}0-9.-]+\.[{_LETTERS}]{{2,}}"
+    rf"|@[{_LETTERS}0-9_]+"
+    rf"|{_ICU_W}+(?:[-_]{_ICU_W}+)*"
+    rf"|[^{_ICU_SPACE}]",
+    regex.VERSION0)
 
 
 def split_words(text: str) -> List[str]:

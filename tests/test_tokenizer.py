@@ -94,6 +94,33 @@ def test_split_words_rules():
     assert split_words("state-of-the-art snake_case 3.5") == ["state-of-the-art", "snake_case", "3", ".", "5", "."]
 
 
+@pytest.mark.parametrize("text,words", [
+    # combining marks are ICU word characters (\p{Mark}): decomposed accents stay in the word
+    ("cafe\u0301 nai\u0308ve", ["cafe\u0301", "nai\u0308ve", "."]),
+    # only decimal digits are ICU word characters: superscripts and fractions split off
+    ("x\u00b2 \u00bd", ["x", "\u00b2", "\u00bd", "."]),
+    # Other_Alphabetic symbols (circled letters) are word characters; lower-cased like Swift
+    ("\u24b6\u24b7", ["\u24d0\u24d1", "."]),
+    # ZWJ / ZWNJ and connector punctuation other than "_" join words
+    ("co\u200dop a\u200cb x\u203fy", ["co\u200dop", "a\u200cb", "x\u203fy", "."]),
+    # \v, U+001C-U+001F and U+0085 are not ICU white space: each is a token of its own
+    ("a\x0bb\x1cc\x85d", ["a", "\x0b", "b", "\x1c", "c", "\x85", "d", "."]),
+    # \p{Z} separators are white space (no-break space, ideographic space, line separator)
+    ("a\u00a0b\u3000c\u2028d", ["a", "b", "c", "d", "."]),
+    # case-insensitive ASCII classes: the Kelvin sign folds to k, long s to s
+    # (the URL runs to the next white space, so it takes the appended sentence end too)
+    ("\u212aelvin@x.io HTTP\u017f://A.b", ["kelvin@x.io", "http\u017f://a.b."]),
+    # CJK and Hangul are alphabetic; full-width punctuation is not
+    ("\u65e5\u672c\u8a9e\uff0c\ud55c\uad6d\uc5b4", ["\u65e5\u672c\u8a9e", "\uff0c", "\ud55c\uad6d\uc5b4", "."]),
+])
+def test_split_words_follows_icu_classes(text, words):
+    """NSRegularExpression is ICU: \\w = [\\p{Alphabetic}\\p{Mark}\\p{Nd}\\p{Pc}\\u200c\\u200d] and
+    \\s = [\\t\\n\\f\\r\\p{Z}] (ICU regular-expression documentation), which differ from
+    Python re's classes on each case here (NativeTokenizer.swift:67-71,198-212)."""
+    from gliner_decide_metal_b200.tokenizer import split_words
+    assert split_words(text) == words
+
+
 def test_schema_layout(tok_dir):
     import gliner_decide_metal_b200 as g
     from gliner_decide_metal_b200.tokenizer import NativeDecisionTokenizer, schema_entries
