@@ -602,9 +602,18 @@ gdc_status gdc_disentangled_attention(const uint16_t* qkv, const uint16_t* pos_q
   int32_t* table = nullptr;
   GDC_TRY(device_error_word(&err));
   GDC_TRY(device_rel_table(&table));
-  return launch_attention(reinterpret_cast<const __half*>(qkv), reinterpret_cast<const __half*>(pos_qk),
-                          reinterpret_cast<const __half*>(key_mask), table, reinterpret_cast<__half*>(ctx), batch,
-                          seq_len, heads, static_cast<cudaStream_t>(stream), err);
+  // the expanded position table of this call, from the stream-ordered allocator
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  __half* pos_exp = nullptr;
+  GDC_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&pos_exp), expanded_position_bytes(heads), s));
+  gdc_status st = launch_expand_positions(reinterpret_cast<const __half*>(pos_qk), table, pos_exp, 2 * heads * 64, s);
+  if (st == GDC_OK)
+    st = launch_attention(reinterpret_cast<const __half*>(qkv), pos_exp, reinterpret_cast<const __half*>(key_mask),
+                          reinterpret_cast<__half*>(ctx), batch, seq_len, heads, s, err);
+  const cudaError_t fe = cudaFreeAsync(pos_exp, s);
+  if (st != GDC_OK) return st;
+  if (fe != cudaSuccess) return set_error(GDC_ERR_CUDA, "cudaFreeAsync: %s", cudaGetErrorString(fe));
+  return GDC_OK;
 }
 
 gdc_status gdc_disentangled_attention_scalar(const uint16_t* qkv, const uint16_t* pos_qk, const uint16_t* key_mask,

@@ -6,32 +6,40 @@
 //   rb[q,k]  = fp16(fp16(c2p + p2c) / fp16(sqrt 192))
 //   s[q,k]   = (q . k) / sqrt(192) + (key valid ? rb : -65504)
 //   ctx[q]   = softmax_k(s) . V
-// with i(r) = clip(bucket(r) + 256, 0, 511) from the 1023-entry table.
+// with i(r) = clip(bucket(r) + 256, 0, 511).
+//
+// Expanded position tables. The kernel reads PQ / PK through the expanded table
+// pos_exp[r + 511] = [PQ | PK][i(r)], r = q - k in [-511, 511] (1023 rows, built once per
+// layer by launch_expand_positions). For a (128-query tile, 128-key tile) pair the distances
+// span r in [q0-k0-127, q0-k0+127], i.e. the 256-row window starting at expanded row
+// lo = q0 - k0 + 384, and in window coordinates the relative terms are pure skews:
+//   C = Q . PKw^T,  c2p[t][kk] = C[t][t - kk + 127]     (own row)
+//   P = K . PQw^T,  p2c[t][kk] = P[kk][t - kk + 127]    (row kk)
+// for every tile pair, log-bucket region included (t, kk: row / key inside the tiles), so the
+// gathers need no index table and their addresses are per-thread constants plus
+// compile-time offsets.
 //
 // Persistent: one CTA per SM takes work items (128-query tile, h, b) one at a time (from an
-// atomic counter, heaviest first, or a static split; see Schedule) and, inside an item,
-// walks the 128-key tiles of the row (tiles whose keys are all padding are skipped: their
-// softmax weight is exactly zero). With packed rows (Schedule::seq_off) a batch row's
-// positions sit at rows seq_off[b] + t of qkv / ctx, query tiles past its extent are never
-// handed out and keys past it get weight zero. For a (query tile, key tile) pair the
-// distances q-k span 255 values, so the needed position rows form one window
-// [lo, lo+256) of PQ / PK.
-// Per pair:
-//   TMA   K, V tiles [128 x 64] (double-buffered) and the PK / PQ windows [256 x 64];
-//         Q [128 x 64] once per item. The next pair's loads (possibly of the next item)
-//         are issued as soon as this pair's gathers are done.
-//   MMA   S = Q K^T (TMEM cols 0-127), C = Q PKw^T (cols 128-383)
-//   rows  drain C -> fp16 in SMEM (row q, 16-byte chunks XOR-swizzled by row)
-//   MMA   P = K PQw^T into cols 128-383
-//   rows  drain P -> fp16 in SMEM (row k) over the consumed windows; gather c2p from the
-//         own row and p2c across rows, add the fp16 relative bias to S, online softmax
-//         (fp32), write fp16 probabilities as a K-major SW128 operand
-//   MMA   O += Prob . V (cols 384-447, V as an MN-major operand); before it the rows
-//         rescale O in TMEM by exp(m_old - m_new) when a row's running max changed
-// Threads: 4 * kParts row warps; warp w owns TMEM lane quarter w % 4 (query rows / key rows
-// 32*(w%4)..+32) and part w / 4 of the columns / keys of every phase. The next warp's lane 0
-// issues the MMAs; the last warp issues the TMA loads (and scans key masks). Every wait is a
-// bounded mbarrier wait; the row warps sleep in theirs.
+// atomic counter, heaviest first, or a static split; see Schedule) and, inside an item, walks
+// the 128-key tiles of the row that hold a valid key (tiles of padding only have exactly zero
+// softmax weight). With packed rows (Schedule::seq_off) a batch row's positions sit at rows
+// seq_off[b] + t of qkv / ctx and query tiles past its extent are never handed out.
+//
+// Roles (one TMA producer warp, one MMA-issuing thread, 8 row warps; row warp w owns TMEM
+// lane quarter w % 4 = query rows / key rows 32*(w%4)..+32 and key part w / 4 = keys
+// 64*(w/4)..+64 of every tile):
+//   TMA   Q per item (double-buffered); per pair K and the PK / PQ windows once the previous
+//         pair's P MMA has consumed them, V once the previous pair's PV has.
+//   MMA   per pair n:  P(n) = K PQw^T after the C drain; then, looking ahead, C(n+1) =
+//         Q PKw^T as soon as P(n) has been drained and the next windows landed (it runs while
+//         the rows score pair n); PV(n) once the probabilities are in TMEM; S(n+1) = Q K^T.
+//         TMEM: S cols 0-127, C / P cols 128-383, O cols 384-447, probabilities 448-511.
+//   rows  drain the C columns their own rows need (the band [t0+64-64p, +96) of 255) to
+//         shared memory, the P rows of their lane quarter over the columns any query row needs
+//         (5 chunks of 32), score their 64 keys in registers (S from TMEM, c2p / p2c from
+//         shared memory), exchange row maxima, exponentiate, write fp16 probabilities to TMEM
+//         (the PV MMA's A operand) and rescale O in TMEM when a row's running max changed.
+// Every wait is a bounded mbarrier wait; the row warps sleep in theirs.
 #pragma once
 
 #include <cuda.h>
@@ -43,52 +51,53 @@
 namespace gdc {
 namespace attn {
 
-constexpr int kTile = 128;      // query rows per item and keys per tile
-constexpr int kWin = 256;       // relative-position window rows per pair
-#ifndef GDC_ATTN_PARTS
-#define GDC_ATTN_PARTS 2
-#endif
-constexpr int kParts = GDC_ATTN_PARTS;   // row warps per TMEM lane quarter (2 or 4)
+constexpr int kTile = 128;       // query rows per item and keys per tile
+constexpr int kWin = 256;        // expanded position rows per pair window
+constexpr int kExpRows = 1023;   // expanded position table rows (r + 511, r in [-511, 511])
+constexpr int kParts = 2;        // row warps per TMEM lane quarter
 constexpr int kRowWarps = 4 * kParts;
-constexpr int kColsPP = 256 / kParts;    // C / P columns drained per row warp
-constexpr int kKeysPP = 128 / kParts;    // keys scored per row warp
-constexpr int kOPP = 64 / kParts;        // O columns accumulated per row warp
+constexpr int kKeysPP = 128 / kParts;   // keys scored per row warp
+constexpr int kOPP = 64 / kParts;       // O columns read per row warp
 constexpr int kRowThreads = kRowWarps * 32;
 constexpr int kThreads = kRowThreads + 64;  // + MMA issuer warp + TMA producer warp
 constexpr int kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColCP = 128, kColO = 384;
+constexpr uint32_t kColS = 0, kColCP = 128, kColO = 384, kColProb = 448;
+
+// C band of one row warp: 32 rows x 96 columns fp16, rows 208 bytes apart (13 chunks of 16 B:
+// the 16-byte drain stores of 32 rows hit distinct bank groups, the skewed 2-byte reads at
+// most two ways).
+constexpr int kCBCols = 96;
+constexpr int kCBPitch = 208;
+constexpr int kCBWarpBytes = 32 * kCBPitch;
+// P band: 128 key rows x 160 columns fp16, rows 336 bytes apart (21 chunks, odd: conflict-free
+// 16-byte drain stores; the reads of one row are contiguous).
+constexpr int kPBCols = 160;
+constexpr int kPBPitch = 336;
 
 // shared memory map (offsets from the 1024-aligned base)
-constexpr int kOffQ = 0;                       // Q tile                16 KB
-constexpr int kOffK = kOffQ + 16384;           // K tiles (2 buffers)   32 KB
-constexpr int kOffV = kOffK + 32768;           // V tiles (2 buffers)   32 KB
-constexpr int kOffW = kOffV + 32768;           // PK | PQ windows 2 x 32 KB, then P rows (64 KB)
-constexpr int kOffC = kOffW + 65536;           // C rows 64 KB, then probabilities (32 KB)
-constexpr int kOffTab = kOffC + 65536;         // relative index table, 1024 x int16
-constexpr int kOffAdd = kOffTab + 2048;        // per item (2 slots) and key: 0 valid, -65504 masked, -inf past
-                                               // the extent; 2 x 512 f32
-constexpr int kOffRed = kOffAdd + 4096;        // cross-part max exchange, 4 x 128 f32
-constexpr int kOffRedL = kOffRed + 2048;       // cross-part denominator exchange, 4 x 128 f32
-constexpr int kOffFlags = kOffRedL + 2048;     // per item (2 slots): key-tile mask, item index, extent, row base
-constexpr int kOffBar = kOffFlags + 64;        // mbarriers
-constexpr int kNumBars = 15;
+constexpr int kOffQ = 0;                                 // Q tiles, 2 x 16 KB
+constexpr int kOffK = kOffQ + 2 * 16384;                 // K tile 16 KB
+constexpr int kOffV = kOffK + 16384;                     // V tile 16 KB
+constexpr int kOffW = kOffV + 16384;                     // PK window 32 KB, then PQ window 32 KB
+constexpr int kOffCB = kOffW + 65536;                    // C bands, 8 x 6.5 KB
+constexpr int kOffPB = kOffCB + kRowWarps * kCBWarpBytes;  // P band 42 KB
+constexpr int kOffBits = kOffPB + 128 * kPBPitch;        // per item slot: 16 words of key-valid bits
+constexpr int kOffRed = kOffBits + 2 * 64;               // cross-part max exchange, kParts x 128 f32
+constexpr int kOffRedL = kOffRed + kParts * 512;         // cross-part denominator exchange
+constexpr int kOffFlags = kOffRedL + kParts * 512;       // per item slot: tile mask, item, extent, row base,
+                                                         // row-has-a-valid-key
+constexpr int kOffBar = kOffFlags + 64;
+enum Bar {
+  kBarFlags = 0, kBarQ0, kBarQ1, kBarQFree0, kBarQFree1, kBarKW, kBarWinFree, kBarV, kBarVFree, kBarC, kBarCDone,
+  kBarP, kBarPDrained, kBarS, kBarProbs, kBarO, kBarODone, kBarRow, kBarDrain, kNumBars
+};
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
-
-enum Bar {
-  kBarQ = 0, kBarKV0, kBarKV1, kBarSC, kBarCDone, kBarP, kBarProbs, kBarO, kBarODone, kBarRow, kBarDrain, kBarFlags,
-  kBarKVFree0, kBarKVFree1, kBarScored
-};
+static_assert(kSmemBytes <= 232448, "attention shared memory exceeds the per-block limit");
 
 constexpr float kInvSqrt192f = 0.07216878364870322f;
 constexpr float kInvScale16 = 1.0f / 13.859375f;  // 1 / fp16(sqrt(192))
-
-// Byte offset of fp16 element (row, col) in a [rows x 256] fp16 block: rows of 512 bytes,
-// 16-byte chunks XOR-swizzled by (row & 7). (col >> 3) << 4 == (2 col) & ~15, and the XOR
-// touches only bits 4-6, so the offset inside a row is (2 col) ^ ((row & 7) << 4).
-__device__ __forceinline__ uint32_t rowblk_off(int row, int col) {
-  return uint32_t(row) * 512u + ((uint32_t(col) << 1) ^ (uint32_t(row & 7) << 4));
-}
+constexpr float kLog2e = 1.4426950408889634f;
 
 // 2^x with the hardware approximation (MUFU.EX2); the exp phase computes
 // exp(s - m) = 2^(s log2 e - m log2 e) with one FFMA per probability.
@@ -110,29 +119,23 @@ struct RowSync {
   }
 };
 
-// kColsPP fp32 TMEM columns of this thread's lane -> fp16, 16-byte stores into the swizzled row.
-__device__ __forceinline__ void drain_rows_f16(uint32_t taddr, uint8_t* base, int row, int col0) {
+// 32 fp32 TMEM columns of this thread's lane -> fp16, four 16-byte stores at byte offsets
+// dst + off(0..3) (off(u) for the u-th group of 8 columns).
+template <typename Off>
+__device__ __forceinline__ void drain32_f16(uint32_t taddr, uint8_t* dst, Off off) {
+  uint32_t r[32];
+  ptx::tmem_ld_32x32b_x32(taddr, r);
+  ptx::tmem_wait_ld();
 #pragma unroll
-  for (int c = 0; c < kColsPP / 32; ++c) {
-    uint32_t r[32];
-    ptx::tmem_ld_32x32b_x32(taddr + uint32_t(c * 32), r);
-    ptx::tmem_wait_ld();
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      uint4 v;
-      v.x = ptx::pack_half2(__uint_as_float(r[u * 8 + 0]), __uint_as_float(r[u * 8 + 1]));
-      v.y = ptx::pack_half2(__uint_as_float(r[u * 8 + 2]), __uint_as_float(r[u * 8 + 3]));
-      v.z = ptx::pack_half2(__uint_as_float(r[u * 8 + 4]), __uint_as_float(r[u * 8 + 5]));
-      v.w = ptx::pack_half2(__uint_as_float(r[u * 8 + 6]), __uint_as_float(r[u * 8 + 7]));
-      *reinterpret_cast<uint4*>(base + rowblk_off(row, col0 + c * 32 + u * 8)) = v;
-    }
+  for (int u = 0; u < 4; ++u) {
+    uint4 v;
+    v.x = ptx::pack_half2(__uint_as_float(r[u * 8 + 0]), __uint_as_float(r[u * 8 + 1]));
+    v.y = ptx::pack_half2(__uint_as_float(r[u * 8 + 2]), __uint_as_float(r[u * 8 + 3]));
+    v.z = ptx::pack_half2(__uint_as_float(r[u * 8 + 4]), __uint_as_float(r[u * 8 + 5]));
+    v.w = ptx::pack_half2(__uint_as_float(r[u * 8 + 6]), __uint_as_float(r[u * 8 + 7]));
+    *reinterpret_cast<uint4*>(dst + off(u)) = v;
   }
 }
-
-__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { ptx::tmem_ld_32x32b_x32(taddr, r); }
-__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[16]) { ptx::tmem_ld_32x32b_x16(taddr, r); }
-__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[32]) { ptx::tmem_st_32x32b_x32(taddr, r); }
-__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[16]) { ptx::tmem_st_32x32b_x16(taddr, r); }
 
 // Work item decomposition: item = (b * heads + h) * n_qt + qt.
 struct Item {
@@ -177,25 +180,33 @@ __device__ __forceinline__ MaskChunk load_mask_chunk(const __half* key_mask, lon
   return c;
 }
 
-// Mask of key tiles to process for a batch row: tiles with a valid key, or every tile when
-// the row has none (the mask then only shifts all scores equally). Executed by a full warp.
-__device__ __forceinline__ uint32_t key_tile_mask(const MaskChunk& c, int n_kt) {
-  uint32_t m = 0;
+// Valid-key byte of this lane for half h: bit j = key (256 h + 8 lane + j) has mask > 0.
+__device__ __forceinline__ uint32_t mask_byte(const MaskChunk& c, int h) {
+  const __half2* p = reinterpret_cast<const __half2*>(&c.v[h]);
+  uint32_t b = 0;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const __half2* p = reinterpret_cast<const __half2*>(&c.v[h]);
-    bool any = false;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __half22float2(p[j]);
-      any |= (f.x > 0.f) | (f.y > 0.f);
-    }
-    const uint32_t bits = __ballot_sync(0xffffffffu, any);  // lanes 0-15: tile 2h, 16-31: tile 2h+1
-    if (bits & 0x0000ffffu) m |= 1u << (2 * h);
-    if (bits & 0xffff0000u) m |= 1u << (2 * h + 1);
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __half22float2(p[j]);
+    b |= (f.x > 0.f ? 1u : 0u) << (2 * j);
+    b |= (f.y > 0.f ? 1u : 0u) << (2 * j + 1);
   }
-  m &= (1u << n_kt) - 1u;
-  return m != 0 ? m : ((1u << n_kt) - 1u);
+  return b;
+}
+
+// The 16 valid-key words of a batch row (word w: keys 32w..32w+31), returned in lanes 0-15
+// (lane w holds word w). Executed by a full warp.
+__device__ __forceinline__ uint32_t mask_words(const MaskChunk& c) {
+  const int lane = int(ptx::lane_id());
+  const uint32_t b0 = mask_byte(c, 0), b1 = mask_byte(c, 1);
+  uint32_t word = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int src = 4 * (lane & 7) + i;
+    const uint32_t v0 = __shfl_sync(0xffffffffu, b0, src);
+    const uint32_t v1 = __shfl_sync(0xffffffffu, b1, src);
+    word |= ((lane & 8) ? v1 : v0) << (8 * i);
+  }
+  return word;
 }
 
 // Work distribution of a launch. Without a counter every CTA takes every gridDim.x-th
@@ -211,22 +222,21 @@ __device__ __forceinline__ int next_tile(uint32_t mask, int kt) {
   return rest ? __ffs(int(rest)) - 1 : -1;
 }
 
-// 4 * kParts + 2 warps per CTA; with kParts = 2 (10 warps) an SM sub-partition holds at
-// most 3 of them, leaving 168 registers per thread.
+// 10 warps per CTA (8 row warps, MMA, TMA); one CTA per SM.
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_pos,
-                        const __half* __restrict__ key_mask, const int32_t* __restrict__ rel_table,
-                        __half* __restrict__ ctx, int B, int L, int heads, int* err, const Schedule sc) {
+                        const __half* __restrict__ key_mask, __half* __restrict__ ctx, int B, int L, int heads,
+                        int* err, const Schedule sc) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  int16_t* s_tab = reinterpret_cast<int16_t*>(sm + kOffTab);
-  float* s_add = reinterpret_cast<float*>(sm + kOffAdd);
+  uint32_t* s_bits = reinterpret_cast<uint32_t*>(sm + kOffBits);
   float* s_red = reinterpret_cast<float*>(sm + kOffRed);
   float* s_red_l = reinterpret_cast<float*>(sm + kOffRedL);
-  volatile uint32_t* s_flags = reinterpret_cast<volatile uint32_t*>(sm + kOffFlags);
-  volatile int32_t* s_item = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 16);
-  volatile int32_t* s_ext = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 32);
-  volatile int32_t* s_row = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 48);
+  volatile uint32_t* s_tmask = reinterpret_cast<volatile uint32_t*>(sm + kOffFlags);
+  volatile int32_t* s_item = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 8);
+  volatile int32_t* s_ext = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 16);
+  volatile int32_t* s_row = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 24);
+  volatile int32_t* s_hasv = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 32);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffTmemSlot);
 
@@ -239,12 +249,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i) ptx::mbar_init(&bars[i], 1);
     ptx::mbar_init(&bars[kBarCDone], kRowWarps);
+    ptx::mbar_init(&bars[kBarPDrained], kRowWarps);
     ptx::mbar_init(&bars[kBarProbs], kRowWarps);
     ptx::mbar_init(&bars[kBarODone], kRowWarps);
     ptx::mbar_init(&bars[kBarRow], kRowThreads);
     ptx::fence_barrier_init();
   }
-  for (int i = threadIdx.x; i < 1023; i += kThreads) s_tab[i] = int16_t(rel_table[i]);
   if (warp == kRowWarps) {
     ptx::tmem_alloc(tmem_slot, kTmemCols);
     ptx::tmem_relinquish();
@@ -254,14 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  auto window_lo = [&](int q0, int k0) {
-    const int lo = s_tab[q0 - (k0 + kTile - 1) + 511];
-    return lo < 512 - kWin ? lo : 512 - kWin;
-  };
   // Packed rows (sc.seq_off != null): batch row b occupies qkv / ctx rows [seq_off[b],
-  // seq_off[b+1]); positions at or past its extent are not computed and items whose query
-  // tile starts past the extent are never handed out. The producer picks the items and
-  // publishes each one (s_item) to the MMA issuer and the row warps.
+  // seq_off[b+1]); items whose query tile starts past the extent are never handed out.
   const int32_t* __restrict__ seq_off = sc.seq_off;
   auto row_base = [&](int b) -> int { return seq_off != nullptr ? seq_off[b] : b * L; };
   auto extent = [&](int b) -> int { return seq_off != nullptr ? seq_off[b + 1] - seq_off[b] : L; };
@@ -296,15 +300,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kRowWarps + 1) {
     // ------------------------------------------------------------ TMA producer warp
-    // Picks the work items (from the launch's counter, or every gridDim.x-th) and publishes
-    // each one with its key-tile mask, extent, first qkv row and additive key mask; loads each
-    // pair's K / V tile (double-buffered) and PK / PQ windows, plus Q per item, as soon as
-    // their buffers are free: the windows and Q once the previous pair's gathers are done
-    // (kBarScored, before its exp phase), the K / V buffer once PV of the pair two back has
-    // completed.
-    uint8_t* sQ = sm + kOffQ;
-    uint8_t* sPK = sm + kOffW;
-    uint8_t* sPQ = sm + kOffW + 32768;
+    // Picks the work items and publishes each one (tile mask, extent, first qkv row,
+    // valid-key bits) at its first pair; loads Q per item into the item's buffer once the
+    // MMAs of the item two back are done with it, each pair's K and PK / PQ windows once the
+    // previous pair's P MMA has completed (its last reader), and V once the previous pair's
+    // PV has.
     if (lane == 0) {
       ptx::prefetch_tensor_map(&tm_qkv);
       ptx::prefetch_tensor_map(&tm_pos);
@@ -323,15 +323,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return __shfl_sync(0xffffffffu, v, 0);
     };
-    int item = fetch(), item_idx = 0, kt = -1, np = 0, loads_issued = 0, q_issued = 0;
-    uint32_t tmask = 0;
-    Item it{};
+    int item = fetch(), ni = 0, np = 0;
     MaskChunk pre{};  // key-mask registers prefetched for the upcoming item (batch row pre_b)
-    int pre_b = -1, pre_ext = 0, pre_row = 0;  // and that row's extent / first qkv row
+    int pre_b = -1, pre_ext = 0, pre_row = 0;
     bool ok = true;
-    while (item >= 0) {
-      // pair np is the first of item `item`: publish its tile mask and load Q
-      it = decode_item(item, n_kt, heads);
+    while (item >= 0 && ok) {
+      const Item it = decode_item(item, n_kt, heads);
       if (pre_b != it.b) {
         pre = load_mask_chunk(key_mask, (long long)it.b * L, L);
         pre_b = it.b;
@@ -339,63 +336,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         pre_row = row_base(it.b);
       }
       const int it_ext = pre_ext, it_row = pre_row;
-      tmask = key_tile_mask(pre, n_kt);
+      const uint32_t words = mask_words(pre);
+      uint32_t tm = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const uint32_t any = __ballot_sync(0xffffffffu, lane < 16 && (lane >> 2) == t && words != 0u);
+        if (any) tm |= 1u << t;
+      }
+      tm &= (1u << n_kt) - 1u;
+      const bool has_valid = tm != 0;
+      const uint32_t tmask = has_valid ? tm : ((1u << n_kt) - 1u);
       int nxt = -1;
       bool first = true;
-      for (kt = next_tile(tmask, -1); kt >= 0; kt = next_tile(tmask, kt)) {
-        if (lane == 0 && np > 0) {
-          // the previous pair's gathers are done (its P rows in the window region and its C
-          // rows are no longer read): windows and Q are free while its exp phase runs
-          ok = ptx::mbar_wait_sleep(&bars[kBarScored], uint32_t((np - 1) & 1), err);
-          // PV of pair np-2, the last reader of this K / V buffer, has completed
-          if (ok && np > 1)
-            ok = ptx::mbar_wait_sleep(&bars[kBarKVFree0 + (np & 1)], uint32_t(((np - 2) >> 1) & 1), err);
-        }
+      for (int kt = next_tile(tmask, -1); kt >= 0 && ok; kt = next_tile(tmask, kt)) {
+        // the previous pair's P MMA has completed: K and the windows are free
+        if (lane == 0 && np > 0) ok = ptx::mbar_wait_sleep(&bars[kBarWinFree], uint32_t((np - 1) & 1), err);
         ok = __shfl_sync(0xffffffffu, ok, 0) != 0;
         if (!ok) break;
+        const int slot = ni & 1;
         if (first) {
-          // the item's additive key mask, one value per key (lane l: keys 8l.. and 256 + 8l..)
-          float* sa = s_add + (item_idx & 1) * 512;
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const __half* mh = reinterpret_cast<const __half*>(&pre.v[hh]);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int k = hh * 256 + lane * 8 + j;
-              sa[k] = k >= it_ext ? -INFINITY : (__half2float(mh[j]) > 0.f ? 0.f : -65504.0f);
+          if (lane < 16) s_bits[slot * 16 + lane] = words;
+          __syncwarp();
+          if (lane == 0) {
+            s_tmask[slot] = tmask;
+            s_item[slot] = item;
+            s_ext[slot] = it_ext;
+            s_row[slot] = it_row;
+            s_hasv[slot] = has_valid ? 1 : 0;
+            ptx::mbar_arrive(&bars[kBarFlags]);  // release: the item is visible to the consumers
+            // Q buffer `slot` is free once the MMAs of item ni - 2 are done with it
+            if (ni >= 2) ok = ptx::mbar_wait_sleep(&bars[kBarQFree0 + slot], uint32_t(((ni - 2) >> 1) & 1), err);
+            if (ok) {
+              ptx::mbar_arrive_expect_tx(&bars[kBarQ0 + slot], 16384);
+              ptx::tma_load_2d(sm + kOffQ + slot * 16384, &tm_qkv, it.h * 64, it_row + it.qt * kTile,
+                               &bars[kBarQ0 + slot]);
             }
           }
-          __syncwarp();
+          ok = __shfl_sync(0xffffffffu, ok, 0) != 0;
+          if (!ok) break;
         }
         if (lane == 0) {
-          if (first) {
-            s_flags[item_idx & 1] = tmask;
-            s_item[item_idx & 1] = item;
-            s_ext[item_idx & 1] = it_ext;
-            s_row[item_idx & 1] = it_row;
-            ptx::mbar_arrive(&bars[kBarFlags]);  // release: mask and item are visible to the consumers
-            ptx::mbar_arrive_expect_tx(&bars[kBarQ], 16384);
-            ptx::tma_load_2d(sQ, &tm_qkv, it.h * 64, it_row + it.qt * kTile, &bars[kBarQ]);
-          }
-          const int buf = np & 1;
           const int k0 = kt * kTile;
-          const int lo = window_lo(it.qt * kTile, k0);
+          const int lo = it.qt * kTile - k0 + 384;  // expanded row of r = q0 - k0 - 127
           const int krow = it_row + k0;
-          uint64_t* bar = &bars[kBarKV0 + buf];
-          ptx::mbar_arrive_expect_tx(bar, 2 * 16384 + 2 * 32768);
-          ptx::tma_load_2d(sm + kOffK + buf * 16384, &tm_qkv, E + it.h * 64, krow, bar);
-          ptx::tma_load_2d(sm + kOffV + buf * 16384, &tm_qkv, 2 * E + it.h * 64, krow, bar);
-          ptx::tma_load_2d(sPK, &tm_pos, E + it.h * 64, lo, bar);
-          ptx::tma_load_2d(sPQ, &tm_pos, it.h * 64, lo, bar);
+          ptx::mbar_arrive_expect_tx(&bars[kBarKW], 16384 + 2 * 32768);
+          ptx::tma_load_2d(sm + kOffK, &tm_qkv, E + it.h * 64, krow, &bars[kBarKW]);
+          ptx::tma_load_2d(sm + kOffW, &tm_pos, E + it.h * 64, lo, &bars[kBarKW]);
+          ptx::tma_load_2d(sm + kOffW + 32768, &tm_pos, it.h * 64, lo, &bars[kBarKW]);
+          // V: free once the previous pair's PV has completed
+          if (np > 0) ok = ptx::mbar_wait_sleep(&bars[kBarVFree], uint32_t((np - 1) & 1), err);
+          if (ok) {
+            ptx::mbar_arrive_expect_tx(&bars[kBarV], 16384);
+            ptx::tma_load_2d(sm + kOffV, &tm_qkv, 2 * E + it.h * 64, krow, &bars[kBarV]);
+          }
         }
+        ok = __shfl_sync(0xffffffffu, ok, 0) != 0;
         if (first) {
-          ++q_issued;
           // the next item, fetched while this pair computes, and its key-mask registers
           nxt = fetch();
           if (nxt >= 0) {
             const int nb = decode_item(nxt, n_kt, heads).b;
             if (nb != pre_b) {
-              pre = load_mask_chunk(key_mask, (long long)nb * L, L);  // consumed at the next item
+              pre = load_mask_chunk(key_mask, (long long)nb * L, L);
               pre_b = nb;
               pre_ext = extent(nb);
               pre_row = row_base(nb);
@@ -403,36 +405,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         first = false;
-        ++loads_issued;
         ++np;
       }
-      if (!ok) break;
       item = nxt;
-      ++item_idx;
-    }
-    if (ok && lane == 0) {
-      // End of the work list: item -1. Published only after the last pair's gathers, so
-      // every consumer has already seen the previous publication (a barrier phase cannot
-      // complete twice ahead of a waiter). The wait is on kBarScored, which this warp has
-      // followed pair by pair: a parity wait is only exact on a barrier at most one phase
-      // ahead of it, and kBarProbs, never waited here before, may still be two behind.
-      if (np == 0 || ptx::mbar_wait_sleep(&bars[kBarScored], uint32_t((np - 1) & 1), err)) {
-        s_flags[item_idx & 1] = 0;
-        s_item[item_idx & 1] = -1;
-        ptx::mbar_arrive(&bars[kBarFlags]);
-      }
+      ++ni;
     }
     if (lane == 0) {
-      // wait (bounded) for the last issued loads to land before the CTA can exit
-      for (int j = loads_issued - 2 < 0 ? 0 : loads_issued - 2; j < loads_issued; ++j) {
+      // End of the work list: item -1, published once the last pair's P MMA has completed
+      // (as every other item: the consumers have seen the previous publication).
+      if (ok && (np == 0 || ptx::mbar_wait_sleep(&bars[kBarWinFree], uint32_t((np - 1) & 1), err))) {
+        s_tmask[ni & 1] = 0;
+        s_item[ni & 1] = -1;
+        ptx::mbar_arrive(&bars[kBarFlags]);
+      }
+      // wait (bounded) for loads that may still be in flight before the CTA can exit
+      if (np > 0) {
         const unsigned long long t1 = ptx::globaltimer();
-        while (!ptx::mbar_try_wait(&bars[kBarKV0 + (j & 1)], uint32_t((j >> 1) & 1)) &&
+        while (!(ptx::mbar_try_wait(&bars[kBarKW], uint32_t((np - 1) & 1)) &&
+                 ptx::mbar_try_wait(&bars[kBarV], uint32_t((np - 1) & 1))) &&
                ptx::globaltimer() - t1 < ptx::kTimeoutNs) {
         }
       }
-      if (q_issued > 0) {
+      for (int j = (ni >= 2 ? ni - 2 : 0); j < ni; ++j) {
         const unsigned long long t2 = ptx::globaltimer();
-        while (!ptx::mbar_try_wait(&bars[kBarQ], uint32_t((q_issued - 1) & 1)) &&
+        while (!ptx::mbar_try_wait(&bars[kBarQ0 + (j & 1)], uint32_t((j >> 1) & 1)) &&
                ptx::globaltimer() - t2 < ptx::kTimeoutNs) {
         }
       }
@@ -443,56 +439,97 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_s = ptx::idesc_f16_f32(128, 128);
       const uint32_t id_cp = ptx::idesc_f16_f32(128, 256);
       const uint32_t id_pv = ptx::idesc_f16_f32(128, 64, 1);
-      const uint32_t aQ = ptx::smem_u32(sm + kOffQ), aPK = ptx::smem_u32(sm + kOffW);
-      const uint32_t aPQ = ptx::smem_u32(sm + kOffW + 32768), aProb = ptx::smem_u32(sm + kOffC);
-      int np = 0, item_idx = 0;
-      bool ok = true;
-      for (; ok; ++item_idx) {
-        if (!ptx::mbar_wait(&bars[kBarFlags], uint32_t(item_idx & 1), err)) break;
-        if (s_item[item_idx & 1] < 0) break;
-        const uint32_t tmask = s_flags[item_idx & 1];
-        bool first = true;
-        for (int kt = next_tile(tmask, -1); kt >= 0; kt = next_tile(tmask, kt), ++np) {
-          const int buf = np & 1;
-          const uint32_t par = uint32_t(np & 1);
-          const bool first_pair = first;
-          ok = ptx::mbar_wait(&bars[kBarKV0 + buf], uint32_t((np >> 1) & 1), err);
-          if (ok && first) ok = ptx::mbar_wait(&bars[kBarQ], uint32_t(item_idx & 1), err);
-          first = false;
+      const uint32_t aK = ptx::smem_u32(sm + kOffK), aV = ptx::smem_u32(sm + kOffV);
+      const uint32_t aPK = ptx::smem_u32(sm + kOffW), aPQ = ptx::smem_u32(sm + kOffW + 32768);
+      auto aQ = [&](int buf) { return ptx::smem_u32(sm + kOffQ + buf * 16384); };
+      auto issue_c = [&](int qbuf) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ptx::umma_f16_ss(tbase + kColCP, ptx::desc_kmajor_sw128(aQ(qbuf) + k * 32),
+                           ptx::desc_kmajor_sw128(aPK + k * 32), id_cp, k > 0);
+        ptx::umma_commit(&bars[kBarC]);
+      };
+      auto issue_s = [&](int qbuf) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ptx::umma_f16_ss(tbase + kColS, ptx::desc_kmajor_sw128(aQ(qbuf) + k * 32),
+                           ptx::desc_kmajor_sw128(aK + k * 32), id_s, k > 0);
+        ptx::umma_commit(&bars[kBarS]);
+      };
+      bool ok = ptx::mbar_wait(&bars[kBarFlags], 0u, err);
+      int ni = 0, np = 0;
+      uint32_t tmask = ok ? s_tmask[0] : 0u;
+      int kt = (ok && s_item[0] >= 0) ? next_tile(tmask, -1) : -1;
+      if (kt >= 0) {
+        // prologue: C(0) and S(0) of the first item
+        ok = ptx::mbar_wait(&bars[kBarKW], 0u, err) && ptx::mbar_wait(&bars[kBarQ0], 0u, err);
+        if (ok) {
+          ptx::tc_fence_after();
+          issue_c(0);
+          issue_s(0);
+        }
+      }
+      bool first_in_item = true;
+      while (ok && kt >= 0) {
+        const uint32_t par = uint32_t(np & 1);
+        // P(np) = K . PQw^T once the rows have drained C(np) out of the shared columns
+        if (!(ok = ptx::mbar_wait(&bars[kBarCDone], par, err))) break;
+        ptx::tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ptx::umma_f16_ss(tbase + kColCP, ptx::desc_kmajor_sw128(aK + k * 32),
+                           ptx::desc_kmajor_sw128(aPQ + k * 32), id_cp, k > 0);
+        ptx::umma_commit(&bars[kBarP]);
+        ptx::umma_commit(&bars[kBarWinFree]);  // K and the windows are free once P(np) completes
+        // look ahead: the next pair, possibly of the next item
+        int nkt = next_tile(tmask, kt);
+        bool new_item = false;
+        uint32_t ntmask = tmask;
+        if (nkt < 0) {
+          if (!(ok = ptx::mbar_wait(&bars[kBarFlags], uint32_t((ni + 1) & 1), err))) break;
+          if (s_item[(ni + 1) & 1] >= 0) {
+            new_item = true;
+            ntmask = s_tmask[(ni + 1) & 1];
+            nkt = next_tile(ntmask, -1);
+          }
+        }
+        const bool has_next = nkt >= 0;
+        const int qbuf = new_item ? ((ni + 1) & 1) : (ni & 1);
+        if (has_next) {
+          // C(np+1) as soon as P(np) has been drained and the next K / windows have landed:
+          // it runs while the rows score pair np
+          ok = ptx::mbar_wait(&bars[kBarKW], uint32_t((np + 1) & 1), err) &&
+               ptx::mbar_wait(&bars[kBarPDrained], par, err) &&
+               (!new_item || ptx::mbar_wait(&bars[kBarQ0 + qbuf], uint32_t(((ni + 1) >> 1) & 1), err));
           if (!ok) break;
           ptx::tc_fence_after();
-          const uint32_t aK = ptx::smem_u32(sm + kOffK + buf * 16384);
-          const uint32_t aV = ptx::smem_u32(sm + kOffV + buf * 16384);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            ptx::umma_f16_ss(tbase + kColS, ptx::desc_kmajor_sw128(aQ + k * 32),
-                             ptx::desc_kmajor_sw128(aK + k * 32), id_s, k > 0);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            ptx::umma_f16_ss(tbase + kColCP, ptx::desc_kmajor_sw128(aQ + k * 32),
-                             ptx::desc_kmajor_sw128(aPK + k * 32), id_cp, k > 0);
-          ptx::umma_commit(&bars[kBarSC]);
-          if (!(ok = ptx::mbar_wait(&bars[kBarCDone], par, err))) break;
-          ptx::tc_fence_after();
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            ptx::umma_f16_ss(tbase + kColCP, ptx::desc_kmajor_sw128(aK + k * 32),
-                             ptx::desc_kmajor_sw128(aPQ + k * 32), id_cp, k > 0);
-          ptx::umma_commit(&bars[kBarP]);
-          // probabilities written and O rescaled to this pair's running max
-          if (!(ok = ptx::mbar_wait(&bars[kBarProbs], par, err))) break;
-          // the previous item's O has been read out of TMEM before this item overwrites it
-          if (first_pair && item_idx > 0 &&
-              !(ok = ptx::mbar_wait(&bars[kBarODone], uint32_t((item_idx - 1) & 1), err)))
-            break;
-          ptx::tc_fence_after();
-#pragma unroll
-          for (int s = 0; s < 8; ++s)
-            ptx::umma_f16_ss(tbase + kColO, ptx::desc_kmajor_sw128(aProb + (s >> 2) * 16384 + (s & 3) * 32),
-                             ptx::desc_mnmajor_sw128(aV + s * 2048), id_pv, (s > 0 || !first_pair) ? 1u : 0u);
-          ptx::umma_commit(&bars[kBarO]);
-          ptx::umma_commit(&bars[kBarKVFree0 + buf]);
+          issue_c(qbuf);
         }
+        // PV(np): probabilities written to TMEM and O rescaled; the previous item's O read out
+        ok = ptx::mbar_wait(&bars[kBarProbs], par, err) && ptx::mbar_wait(&bars[kBarV], par, err) &&
+             (!first_in_item || ni == 0 || ptx::mbar_wait(&bars[kBarODone], uint32_t((ni - 1) & 1), err));
+        if (!ok) break;
+        ptx::tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          ptx::umma_f16_ts(tbase + kColO, tbase + kColProb + uint32_t(8 * s), ptx::desc_mnmajor_sw128(aV + s * 2048),
+                           id_pv, (s > 0 || !first_in_item) ? 1u : 0u);
+        ptx::umma_commit(&bars[kBarO]);
+        ptx::umma_commit(&bars[kBarVFree]);
+        if (has_next) {
+          // S(np+1): the rows have consumed S(np) (their probabilities are written)
+          issue_s(qbuf);
+          if (new_item) ptx::umma_commit(&bars[kBarQFree0 + (ni & 1)]);  // item ni's Q reads are issued
+        }
+        ++np;
+        if (new_item) {
+          ++ni;
+          tmask = ntmask;
+          first_in_item = true;
+        } else {
+          first_in_item = false;
+        }
+        kt = nkt;
       }
       // drain outstanding tensor-core work before TMEM is released
       ptx::umma_commit(&bars[kBarDrain]);
@@ -504,92 +541,120 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- row threads
     const int quarter = warp & 3;
     const int part = warp >> 2;
-    const int t = quarter * 32 + lane;  // TMEM lane; query row q0 + t; key row k0 + t
-    const uint32_t lane_base = tbase + (uint32_t(quarter * 32) << 16);
-    uint8_t* sC = sm + kOffC;
-    uint8_t* sPst = sm + kOffW;
-    const uint32_t c_row = uint32_t(t) * 512u;
-    const uint32_t c_xor = uint32_t(t & 7) << 4;
+    const int t0 = quarter * 32;
+    const int t = t0 + lane;  // TMEM lane; query row q0 + t; key row k0 + t
+    const uint32_t lane_base = tbase + (uint32_t(t0) << 16);
+    uint8_t* cband = sm + kOffCB + warp * kCBWarpBytes;
+    uint8_t* pband = sm + kOffPB;
+    // C band of this warp: window columns [cb0, cb0 + 96); c2p(t, 64 part + j) is band column
+    // lane - j + 63 of this lane's row
+    const int cb0 = t0 + 64 - 64 * part;
+    const uint8_t* c2p_base = cband + lane * kCBPitch + 2 * (lane + 63);
+    // P band row kk holds window columns [96 - 32 (kk / 32), +160); p2c(t, kk) is its column
+    // t + 31 - kk % 32
+    const uint8_t* p2c_base = pband + 2 * (t + 31) + part * 64 * kPBPitch;
     RowSync rs{&bars[kBarRow]};
     int np = 0;
-    int item_idx = 0;
     bool ok = true;
-    for (; ok; ++item_idx) {
-      if (!ptx::mbar_wait_sleep(&bars[kBarFlags], uint32_t(item_idx & 1), err)) {
+    for (int ni = 0; ok; ++ni) {
+      if (!ptx::mbar_wait_sleep(&bars[kBarFlags], uint32_t(ni & 1), err)) {
         ok = false;
         break;
       }
-      const int item = s_item[item_idx & 1];
+      const int slot = ni & 1;
+      const int item = s_item[slot];
       if (item < 0) break;
-      const uint32_t tmask = s_flags[item_idx & 1];
+      const uint32_t tmask = s_tmask[slot];
+      const bool has_valid = s_hasv[slot] != 0;
       const Item it = decode_item(item, n_kt, heads);
-      const int q0 = it.qt * kTile;
-      const int q = q0 + t;
-      const long long orow0 = s_row[item_idx & 1];  // qkv / ctx row of position 0
-      const int ext = s_ext[item_idx & 1];
-      const float* s_add_item = s_add + (item_idx & 1) * 512;
+      const int q = it.qt * kTile + t;
+      const long long orow0 = s_row[slot];  // qkv / ctx row of position 0
+      const int ext = s_ext[slot];
       float m_run = -INFINITY, l_part = 0.f;
       bool first_pair = true;
       for (int kt = next_tile(tmask, -1); kt >= 0; kt = next_tile(tmask, kt), ++np) {
-        const int k0 = kt * kTile;
-        const int lo = window_lo(q0, k0);
         const uint32_t par = uint32_t(np & 1);
-        const float* s_add_pair = s_add_item + k0;
-        // ---- drain C (own query row, this part's 64 columns)
-        if (!ptx::mbar_wait_sleep(&bars[kBarSC], par, err)) {
+        // this part's 64 keys: valid bits; a part with none is skipped (its probabilities
+        // are exactly zero) unless the row has no valid key at all
+        const int kw = (kt * kTile + part * kKeysPP) >> 5;
+        const uint32_t vb0 = s_bits[slot * 16 + kw], vb1 = s_bits[slot * 16 + kw + 1];
+        const bool live = !has_valid || (vb0 | vb1) != 0u;
+        // the P rows of this lane quarter are read only by the part that owns their keys
+        const int pq_part = quarter >> 1;
+        const int pkw = (kt * kTile + pq_part * kKeysPP) >> 5;
+        const bool p_live = !has_valid || (s_bits[slot * 16 + pkw] | s_bits[slot * 16 + pkw + 1]) != 0u;
+        // ---- drain C: the band of window columns this warp's rows need
+        if (!ptx::mbar_wait_sleep(&bars[kBarC], par, err)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
-        drain_rows_f16(lane_base + kColCP + part * kColsPP, sC, t, part * kColsPP);
+        if (live) {
+#pragma unroll
+          for (int c = 0; c < 3; ++c)
+            drain32_f16(lane_base + kColCP + uint32_t(cb0 + 32 * c), cband + lane * kCBPitch,
+                        [&](int u) { return (4 * c + u) * 16; });
+        }
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&bars[kBarCDone]);
-        // ---- drain P (own key row) over the consumed windows
+        // ---- drain P: rows of this lane quarter, window columns [96 - t0, 256 - t0)
         if (!ptx::mbar_wait_sleep(&bars[kBarP], par, err)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
-        drain_rows_f16(lane_base + kColCP + part * kColsPP, sPst, t, part * kColsPP);
+        if (p_live) {
+#pragma unroll
+          for (int c = part; c < 5; c += kParts)
+            drain32_f16(lane_base + kColCP + uint32_t(96 - t0 + 32 * c), pband + t * kPBPitch,
+                        [&](int u) { return (4 * c + u) * 16; });
+        }
         ptx::tc_fence_before();
-        if (!rs.sync(err)) {
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&bars[kBarPDrained]);
+        if (!rs.sync(err)) {  // every P row is in shared memory
           ok = false;
           break;
         }
-        // ---- scores of keys [part*kKeysPP, +kKeysPP) with the gathered relative bias
-        const int16_t* tab_q = s_tab + (q - k0 + 511);  // tab_q[-kk] = i(q - (k0 + kk))
-        // final scores go back into this lane's S columns (TMEM), not registers
+        // ---- scores of keys [64 part, +64) with the gathered relative bias, in registers
+        if (!ptx::mbar_wait_sleep(&bars[kBarS], par, err)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        float s[kKeysPP];
         float part_max = -INFINITY;
+        if (live) {
 #pragma unroll
-        for (int c = 0; c < kKeysPP / 32; ++c) {
-          uint32_t sraw[32];
-          ptx::tmem_ld_32x32b_x32(lane_base + kColS + part * kKeysPP + c * 32, sraw);
-          ptx::tmem_wait_ld();
+          for (int c = 0; c < kKeysPP / 32; ++c) {
+            uint32_t sraw[32];
+            ptx::tmem_ld_32x32b_x32(lane_base + kColS + uint32_t(part * kKeysPP + c * 32), sraw);
+            ptx::tmem_wait_ld();
+            const uint32_t vb = c == 0 ? vb0 : vb1;
 #pragma unroll
-          for (int u = 0; u < 32; ++u) {
-            const int kk = part * kKeysPP + c * 32 + u;
-            const uint32_t w2 = uint32_t(int(tab_q[-kk]) - lo) << 1;  // 2 * window column
-            const __half cv = *reinterpret_cast<const __half*>(sC + c_row + (w2 ^ c_xor));
-            const __half pv =
-                *reinterpret_cast<const __half*>(sPst + uint32_t(kk) * 512u + (w2 ^ (uint32_t(kk & 7) << 4)));
-            const float rb = __half2float(__float2half_rn(__half2float(__hadd(cv, pv)) * kInvScale16));
-            const float add = s_add_pair[kk];
-            const float sv = fmaf(__uint_as_float(sraw[u]), kInvSqrt192f, add == 0.f ? rb : add);
-            sraw[u] = __float_as_uint(sv);
-            part_max = fmaxf(part_max, sv);
+            for (int u = 0; u < 32; ++u) {
+              const int j = c * 32 + u;
+              // c2p: own row, band column lane - j + 63; p2c: P row 64 part + j, column
+              // t + 31 - (j % 32)
+              const __half cv = *reinterpret_cast<const __half*>(c2p_base - 2 * j);
+              const __half pv = *reinterpret_cast<const __half*>(p2c_base + j * kPBPitch - 2 * (j & 31));
+              const float rb = __half2float(__float2half_rn(__half2float(__hadd(cv, pv)) * kInvScale16));
+              const float sv = fmaf(__uint_as_float(sraw[u]), kInvSqrt192f, ((vb >> u) & 1u) ? rb : -65504.0f);
+              s[j] = sv;
+              part_max = fmaxf(part_max, sv);
+            }
           }
-          ptx::tmem_st_32x32b_x32(lane_base + kColS + part * kKeysPP + c * 32, sraw);
+        } else {
+#pragma unroll
+          for (int j = 0; j < kKeysPP; ++j) s[j] = -INFINITY;
         }
-        ptx::tmem_wait_st();
         s_red[part * 128 + t] = part_max;
-        // every row is past its C / P reads (probabilities overwrite the C rows, the next
-        // pair's windows the P rows) and all parts' maxima are visible
+        // every row is past its C / P band reads and all parts' maxima are visible
         if (!rs.sync(err)) {
           ok = false;
           break;
         }
-        if (threadIdx.x == 0) ptx::mbar_arrive(&bars[kBarScored]);  // the producer may load the next windows
         float m_tile = s_red[t];
 #pragma unroll
         for (int pp = 1; pp < kParts; ++pp) m_tile = fmaxf(m_tile, s_red[pp * 128 + t]);
@@ -598,51 +663,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the softmax denominator sums the fp32 exponentials (the reference's SDPA softmax is
         // fp32); the PV MMA multiplies their fp16 roundings
         float psum = 0.f;
-        const float m_l2 = m_new * 1.4426950408889634f;
+        const float m_l2 = m_new * kLog2e;
+        uint32_t pk[kKeysPP / 2];
 #pragma unroll
-        for (int c = 0; c < kKeysPP / 32; ++c) {
-          uint32_t sv[32];
-          ptx::tmem_ld_32x32b_x32(lane_base + kColS + part * kKeysPP + c * 32, sv);
-          ptx::tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t pk[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = j * 8 + 2 * e;
-              const float e0 = ex2_approx(fmaf(__uint_as_float(sv[i]), 1.4426950408889634f, -m_l2));
-              const float e1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), 1.4426950408889634f, -m_l2));
-              const __half2 p2 = __floats2half2_rn(e0, e1);
-              psum += e0 + e1;
-              pk[e] = *reinterpret_cast<const uint32_t*>(&p2);
-            }
-            // K-major SW128 operand: atom kb / 64 holds keys 64*(kb/64)..+63 of row t
-            const int kb = part * kKeysPP + c * 32 + j * 8;
-            const uint32_t ch = uint32_t((kb & 63) >> 3);
-            const uint32_t off = uint32_t(kb >> 6) * 16384u + uint32_t(t >> 3) * 1024u + uint32_t(t & 7) * 128u +
-                                 ((ch ^ uint32_t(t & 7)) << 4);
-            *reinterpret_cast<uint4*>(sC + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          }
+        for (int i = 0; i < kKeysPP / 2; ++i) {
+          const float e0 = ex2_approx(fmaf(s[2 * i], kLog2e, -m_l2));
+          const float e1 = ex2_approx(fmaf(s[2 * i + 1], kLog2e, -m_l2));
+          psum += e0 + e1;
+          pk[i] = ptx::pack_half2(e0, e1);
         }
-        ptx::fence_proxy_async_smem();
-        // ---- O accumulates in TMEM across the item's pairs: rescale it to the new running
-        // max before this pair's PV (skipped when no row of the warp changed its max)
-        if (!first_pair) {
-          if (!ptx::mbar_wait_sleep(&bars[kBarO], par ^ 1u, err)) {  // PV of the previous pair done
+        // PV of the previous pair has completed: the probability columns are free and O holds
+        // every earlier pair of this item
+        if (np > 0) {
+          if (!ptx::mbar_wait_sleep(&bars[kBarO], par ^ 1u, err)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          if (!__all_sync(0xffffffffu, alpha == 1.0f)) {
-            uint32_t r[kOPP];
-            tmem_ld_cols(lane_base + kColO + part * kOPP, r);
-            ptx::tmem_wait_ld();
-#pragma unroll
-            for (int u = 0; u < kOPP; ++u) r[u] = __float_as_uint(__uint_as_float(r[u]) * alpha);
-            tmem_st_cols(lane_base + kColO + part * kOPP, r);
-            ptx::tmem_wait_st();
-          }
         }
+        if (!first_pair && !__all_sync(0xffffffffu, alpha == 1.0f)) {
+          uint32_t r[kOPP];
+          ptx::tmem_ld_32x32b_x32(lane_base + kColO + uint32_t(part * kOPP), r);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < kOPP; ++u) r[u] = __float_as_uint(__uint_as_float(r[u]) * alpha);
+          ptx::tmem_st_32x32b_x32(lane_base + kColO + uint32_t(part * kOPP), r);
+        }
+        ptx::tmem_st_32x32b_x32(lane_base + kColProb + uint32_t(part * (kKeysPP / 2)), pk);
+        ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&bars[kBarProbs]);
@@ -660,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float o[kOPP];
       {
         uint32_t r[kOPP];
-        tmem_ld_cols(lane_base + kColO + part * kOPP, r);
+        ptx::tmem_ld_32x32b_x32(lane_base + kColO + uint32_t(part * kOPP), r);
         ptx::tmem_wait_ld();
 #pragma unroll
         for (int u = 0; u < kOPP; ++u) o[u] = __uint_as_float(r[u]);
@@ -668,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&bars[kBarODone]);
-      // combine the parts' softmax denominators and store this part's 16 columns
+      // combine the parts' softmax denominators and store this part's 32 columns
       s_red_l[part * 128 + t] = l_part;
       if (!rs.sync(err)) {
         ok = false;
@@ -706,6 +754,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       atomicExch(sc.counter + 1, 0);
     }
   }
+}
+
+// pos_exp[x] = pos_qk[rel_table[x]] for x in [0, 1023): one row of 2E fp16 per block.
+__global__ void expand_positions_kernel(const __half* __restrict__ pos_qk, const int32_t* __restrict__ rel_table,
+                                        __half* __restrict__ pos_exp, int cols) {
+  const int x = blockIdx.x;
+  const int src = rel_table[x];
+  const uint4* s = reinterpret_cast<const uint4*>(pos_qk + size_t(src) * size_t(cols));
+  uint4* d = reinterpret_cast<uint4*>(pos_exp + size_t(x) * size_t(cols));
+  for (int i = threadIdx.x; i < cols / 8; i += blockDim.x) d[i] = s[i];
 }
 
 }  // namespace attn

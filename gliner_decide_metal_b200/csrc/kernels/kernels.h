@@ -70,11 +70,20 @@ struct AttentionWork {
   int* counter = nullptr;
 };
 
-// Disentangled attention over the fused QKV projection output (see gdc.h).
-// rel_table: 1023 int32 gather indices (device).
-gdc_status launch_attention(const __half* qkv, const __half* pos_qk, const __half* key_mask,
-                            const int32_t* rel_table, __half* ctx, int batch, int seq_len, int heads,
-                            cudaStream_t stream, int* err, const AttentionWork& work = AttentionWork{});
+// Disentangled attention over the fused QKV projection output (see gdc.h). pos_exp: the
+// expanded position table of launch_expand_positions ([1023, 2 * heads * 64] fp16, device).
+gdc_status launch_attention(const __half* qkv, const __half* pos_exp, const __half* key_mask, __half* ctx,
+                            int batch, int seq_len, int heads, cudaStream_t stream, int* err,
+                            const AttentionWork& work = AttentionWork{});
+
+// Expanded position table: pos_exp[x] = pos_qk[rel_table[x]] for x in [0, 1023), rows of
+// `cols` fp16 (cols = 2 * heads * 64: PQ | PK). rel_table: the 1023 gather indices i(r),
+// index r + 511 (device). Row x holds the relative projections of distance r = x - 511.
+gdc_status launch_expand_positions(const __half* pos_qk, const int32_t* rel_table, __half* pos_exp, int cols,
+                                   cudaStream_t stream);
+
+// Bytes of an expanded position table for `heads` heads.
+inline size_t expanded_position_bytes(int heads) { return size_t(1023) * size_t(2 * heads * 64) * 2; }
 
 // rows[r] = hidden[marker[r] + (r / per_batch) * seq_len] (DeBERTa.swift:430-436).
 // Marker indices outside [0, seq_len) set kErrBadMarkerIndex and read row 0 of the batch.

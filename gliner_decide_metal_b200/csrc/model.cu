@@ -195,7 +195,8 @@ gdc_status model_load(const char* path, const gdc_config* cfg_in, int device, gd
   size_t total = 0;
   for (auto& u : ups) total += align256(u.host.size() * 2);
   const size_t pos_bytes = align256(size_t(512) * 2 * E * 2);
-  total += pos_bytes * size_t(cfg.num_hidden_layers);
+  const size_t exp_bytes = align256(size_t(1023) * 2 * E * 2);
+  total += (pos_bytes + exp_bytes) * size_t(cfg.num_hidden_layers);
   total += align256(E * 2) * 2 + align256(size_t(512) * E * 2) + align256(1023 * 4) + 256;
 
   auto fail = [&](gdc_status s) {
@@ -227,6 +228,8 @@ gdc_status model_load(const char* path, const gdc_config* cfg_in, int device, gd
   for (auto& L : m->layers) {
     L.pos_qk = reinterpret_cast<__half*>(cur);
     cur += pos_bytes;
+    L.pos_exp = reinterpret_cast<__half*>(cur);
+    cur += exp_bytes;
   }
   __half* rel_g_d = reinterpret_cast<__half*>(cur);
   cur += align256(E * 2);
@@ -253,6 +256,8 @@ gdc_status model_load(const char* path, const gdc_config* cfg_in, int device, gd
   for (auto& L : m->layers) {
     st = launch_linear(rel_norm, E, L.wqkv, L.bqkv, L.pos_qk, 2 * E, 512, int(2 * E), int(E), kActNone, m->stream,
                        m->err);
+    if (st != GDC_OK) return fail(st);
+    st = launch_expand_positions(L.pos_qk, m->rel_table, L.pos_exp, int(2 * E), m->stream);
     if (st != GDC_OK) return fail(st);
   }
   // keep LN(rel) as the model's relative table copy (rel_ln aliases the raw upload slot)
@@ -415,7 +420,7 @@ gdc_status enqueue_forward(gdc_model* m, int B, int L, int Hm, int O, const int3
     const std::string p = rec.named ? "layer_" + std::to_string(i) + "_" : std::string();
     GDC_TRY(launch_linear(w.x, E, Lw.wqkv, Lw.bqkv, w.big, 3 * E, T, 3 * E, E, kActNone, s, m->err, m_dev));
     rec.end(kProfQkvGemm, p + "attention_projection");
-    GDC_TRY(launch_attention(w.big, Lw.pos_qk, mask, m->rel_table, w.ctx, B, L, m->heads, s, m->err, work));
+    GDC_TRY(launch_attention(w.big, Lw.pos_exp, mask, w.ctx, B, L, m->heads, s, m->err, work));
     rec.end(kProfAttention, p + "attention");
     GDC_TRY(launch_linear(w.ctx, E, Lw.wo, Lw.bo, w.tmp, E, T, E, E, kActNone, s, m->err, m_dev));
     rec.end(kProfOutGemm, "");

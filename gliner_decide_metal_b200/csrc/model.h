@@ -28,6 +28,7 @@ struct LayerWeights {
   __half* ln2_g = nullptr;
   __half* ln2_b = nullptr;
   __half* pos_qk = nullptr;  // [512, 2E]: PQ | PK (DeBERTa.swift:218-227)
+  __half* pos_exp = nullptr; // [1023, 2E]: pos_exp[r + 511] = pos_qk[i(r)] (attention's expanded table)
 };
 
 // Kernel groups recorded by the stage profiler.

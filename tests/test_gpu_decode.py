@@ -84,13 +84,17 @@ def test_decode_device_matches_reference_rules_and_host_decode():
     assert np.array_equal(sel, hs)
     # probabilities: float64 results stored as float32
     assert np.abs(probs.astype(np.float64) - hp).max() <= 1e-6
-    # the oracle's restatement, task by task
+    # the oracle's restatement, task by task (the reference decodes only tasks that have labels;
+    # a slot with n_labels = 0 stays empty)
     for b in range(B):
-        for (p_ref, sel_ref), h in zip(rf.decode(logits[b], n_labels[b], multi[b]), range(Hm)):
+        for h in range(Hm):
             n = int(n_labels[b, h])
+            assert not sel[b, h, n:].any() and not probs[b, h, n:].any()
+            if n == 0:
+                continue
+            (p_ref, sel_ref), = rf.decode(logits[b, h:h + 1], [n], [int(multi[b, h])])
             np.testing.assert_allclose(probs[b, h, :n], p_ref, rtol=0, atol=1e-6)
             assert sorted(np.flatnonzero(sel[b, h, :n]).tolist()) == sorted(sel_ref), (b, h)
-            assert not sel[b, h, n:].any() and not probs[b, h, n:].any()
     # the hand-made rows
     assert sel[0, 0, :4].tolist() == [1, 1, 1, 1]
     assert sel[0, 1, :5].tolist() == [0, 1, 0, 0, 0]
