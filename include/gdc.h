@@ -292,19 +292,23 @@ gdc_status gdc_disentangled_attention_scalar(const uint16_t* qkv, const uint16_t
  * reference. Same arguments, layout and results. It is for callers that cannot let a
  * library call cudaMalloc: hosts that reserve all device memory for their own pool up
  * front, or that must not take the implicit device synchronisation and address-space
- * change of an allocation in the middle of their run. The kernel's scratch (the relative
- * index table and a status word, 4352 bytes) is a file-scope __device__ array that every
- * device loading this library holds until the process exits; nothing here calls
- * cudaMalloc, cudaFree or an allocating library routine.
- *  - Limit: seq_len <= 512 (the table in the static array covers |q - k| <= 511);
- *    larger values return GDC_ERR_UNSUPPORTED. heads must be 16.
+ * change of an allocation in the middle of their run. The scratch that
+ * gdc_disentangled_attention allocates (the expanded position table of the call, rebuilt
+ * from pos_qk by every call, the relative index table and a status word; 4,194,560 bytes in
+ * all) is a file-scope __device__ array that every device loading this library holds until
+ * the process exits; nothing here calls cudaMalloc, cudaFree or an allocating library
+ * routine.
+ *  - Limit: heads must be 16 (the array holds one 1023 x 2048 table) and seq_len <= 512
+ *    (the table covers |q - k| <= 511); other values return GDC_ERR_UNSUPPORTED.
  *  - The first call on a device sets the array up (resolves its device address and
- *    copies the table in, synchronously); make that first call before any stream capture.
- *  - Each call clears the status word on `stream`, launches, reads the status word back
- *    and synchronises `stream`, so it returns once the kernel has finished; a bounded-wait
- *    timeout is returned as GDC_ERR_TIMEOUT.
+ *    copies the relative index table in, synchronously); make that first call before any
+ *    stream capture.
+ *  - Each call clears the status word on `stream`, expands pos_qk into the array, launches,
+ *    reads the status word back and synchronises `stream`, so it returns once the kernel has
+ *    finished; a bounded-wait timeout is returned as GDC_ERR_TIMEOUT.
  *  - All calls on a device share the array and it keeps the last call's contents. Calls
- *    that overlap on the GPU (different streams or host threads) race on the status word. */
+ *    that overlap on the GPU (different streams or host threads) race on the expanded
+ *    table and the status word. */
 gdc_status gdc_disentangled_attention_noalloc(const uint16_t* qkv, const uint16_t* pos_qk,
                                               const uint16_t* key_mask, uint16_t* ctx, int32_t batch,
                                               int32_t seq_len, int32_t heads, void* stream);
