@@ -284,6 +284,221 @@ gdc_status launch_gemm_variant(const CUtensorMap& ta, const CUtensorMap& tw, con
   return check_launch("gemm_tn_kernel");
 }
 
+// ------------------------------------------------------------------ skinny path (M <= 128)
+//
+// With at most 128 rows (a batch of one short row: BASELINE config 0 has M = 32) a GEMM is
+// weight streaming: every weight byte is read once and the arithmetic is small. One
+// persistent CTA per 256-column tile (the kernel above) leaves most SMs idle, each of the
+// few busy ones streaming megabytes alone. Here every CTA owns one narrow column tile
+// (BN = 16, 32 or 64 columns) over all of K, so 64-148 CTAs stream the weights at once:
+//   warp 0 lane 0  TMA: per 128-column K block, the A rows [round_up(M, 8) x 128] (rows past
+//                  that stay stale in shared memory: the MMA rows they feed are not stored)
+//                  and the W tile [BN x 128], into an S-deep ring;
+//   warp 1 lane 0  tcgen05.mma M=128, N=BN, K=16 (8 per K block) into one TMEM accumulator;
+//   warps 0-3      epilogue: TMEM lane quarter w, rows 32w..32w+31 below M: bias, GELU / ReLU,
+//                  fp16, 16-byte stores.
+// Each output element is one accumulation chain over K in order, as in the kernels above.
+constexpr int kSkBK = 128;
+constexpr int kSkThreads = 128;
+
+template <int BN>
+struct SkinnyShape {
+  static constexpr int kAAtom = 128 * 64 * 2;  // 128 MMA rows x 64 K, 128-byte swizzle
+  static constexpr int kBAtom = BN * 64 * 2;
+  static constexpr int kStageBytes = 2 * kAAtom + 2 * kBAtom;
+  static constexpr int kStages = (200 * 1024) / kStageBytes < 8 ? (200 * 1024) / kStageBytes : 8;
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+template <int BN, int ACT>
+__global__ void __launch_bounds__(kSkThreads, 1)
+    gemm_skinny_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                       const __half* __restrict__ bias, __half* __restrict__ out, int M_cap, int K, long long ldo,
+                       int a_box_rows, int* err, const int32_t* __restrict__ m_dev) {
+  using S = SkinnyShape<BN>;
+  const int M = m_dev != nullptr ? min(M_cap, *m_dev) : M_cap;  // rows stored
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
+  uint64_t* empty = full + S::kStages;
+  uint64_t* done = empty + S::kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int kblocks = (K + kSkBK - 1) / kSkBK;  // a last half block reads TMA zero fill
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::kStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    ptx::mbar_init(done, 1);
+    ptx::fence_barrier_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, S::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  auto stage_a = [&](int s) { return smem + s * S::kStageBytes; };
+  auto stage_b = [&](int s) { return smem + s * S::kStageBytes + 2 * S::kAAtom; };
+
+  bool ok = true;
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tensor_map(&tm_a);
+    ptx::prefetch_tensor_map(&tm_w);
+    const uint32_t tx = 2u * uint32_t(a_box_rows * 128 + S::kBAtom);
+    int issued = 0;
+    for (int kb = 0; kb < kblocks && ok; ++kb) {
+      const int s = kb % S::kStages;
+      if (!(ok = ptx::mbar_wait(&empty[s], uint32_t(((kb / S::kStages) & 1) ^ 1), err))) break;
+      ptx::mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        ptx::tma_load_2d(stage_a(s) + h * S::kAAtom, &tm_a, kb * kSkBK + h * 64, 0, &full[s]);
+        ptx::tma_load_2d(stage_b(s) + h * S::kBAtom, &tm_w, kb * kSkBK + h * 64, n0, &full[s]);
+      }
+      ++issued;
+    }
+    // loads still in flight land before the CTA can exit (bounded)
+    for (int j = issued - S::kStages < 0 ? 0 : issued - S::kStages; j < issued; ++j) {
+      const unsigned long long t0 = ptx::globaltimer();
+      while (!ptx::mbar_try_wait(&full[j % S::kStages], uint32_t((j / S::kStages) & 1)) &&
+             ptx::globaltimer() - t0 < ptx::kTimeoutNs) {
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = ptx::idesc_f16_f32(128, BN);
+    for (int kb = 0; kb < kblocks; ++kb) {
+      const int s = kb % S::kStages;
+      if (!(ok = ptx::mbar_wait(&full[s], uint32_t((kb / S::kStages) & 1), err))) break;
+      ptx::tc_fence_after();
+      const uint32_t a_addr = ptx::smem_u32(stage_a(s)), b_addr = ptx::smem_u32(stage_b(s));
+#pragma unroll
+      for (int k = 0; k < kSkBK / 16; ++k)
+        ptx::umma_f16_ss(tmem_base, ptx::desc_kmajor_sw128(a_addr + (k >> 2) * S::kAAtom + (k & 3) * 32),
+                         ptx::desc_kmajor_sw128(b_addr + (k >> 2) * S::kBAtom + (k & 3) * 32), idesc,
+                         (kb | k) != 0 ? 1u : 0u);
+      ptx::umma_commit(&empty[s]);
+    }
+    // `done` also drains every issued MMA before TMEM is released
+    ptx::umma_commit(done);
+  }
+  __syncwarp();
+  // ---- epilogue: rows 32 warp + lane below M
+  // (warp-uniform: the TMEM load below is a warp-collective instruction)
+  const bool have = __all_sync(0xffffffffu, ptx::mbar_wait_sleep(done, 0u, err));
+  ptx::tc_fence_after();
+  const int row = warp * 32 + lane;
+  if (have) {
+#pragma unroll
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t r[16];
+      ptx::tmem_ld_32x32b_x16(tmem_base + (uint32_t(warp * 32) << 16) + uint32_t(c0), r);
+      ptx::tmem_wait_ld();
+      if (row < M) {
+        uint32_t packed[8];
+        const uint4* bsrc = reinterpret_cast<const uint4*>(bias + n0 + c0);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const uint4 bv = __ldg(bsrc + q);
+          const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 bf = __half22float2(bh[j]);
+            float v0 = __uint_as_float(r[q * 8 + 2 * j]) + bf.x;
+            float v1 = __uint_as_float(r[q * 8 + 2 * j + 1]) + bf.y;
+            if (ACT == kActGelu) {
+              v0 = gelu_erf(v0);
+              v1 = gelu_erf(v1);
+            } else if (ACT == kActRelu) {
+              v0 = fmaxf(v0, 0.f);
+              v1 = fmaxf(v1, 0.f);
+            }
+            packed[q * 4 + j] = ptx::pack_half2(v0, v1);
+          }
+        }
+        uint4* dst = reinterpret_cast<uint4*>(out + (long long)row * ldo + n0 + c0);
+        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+      }
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, S::kTmemCols);
+  }
+}
+
+template <int BN, int ACT>
+gdc_status launch_skinny_variant(const CUtensorMap& ta, const CUtensorMap& tw, const __half* bias, __half* out,
+                                 long long ldo, int M, int N, int K, int a_box_rows, cudaStream_t stream, int* err,
+                                 const int32_t* m_dev) {
+  using S = SkinnyShape<BN>;
+  auto kern = gemm_skinny_kernel<BN, ACT>;
+  static PerDeviceOnce configured;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return set_error(GDC_ERR_CUDA, "device ordinal out of range");
+  const cudaError_t ce = cudaError_t(per_device_once(configured, dev, [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
+  }));
+  if (ce != cudaSuccess) return set_error(GDC_ERR_CUDA, "skinny gemm smem attribute: %s", cudaGetErrorString(ce));
+  kern<<<N / BN, kSkThreads, S::kSmemBytes, stream>>>(ta, tw, bias, out, M, K, ldo, a_box_rows, err, m_dev);
+  return check_launch("gemm_skinny_kernel");
+}
+
+// Column tile of the skinny path: the estimated time of a launch is its waves over the SMs
+// times the bytes one CTA streams (its W columns plus all of A); the narrowest tile wins ties.
+int choose_skinny_bn(int64_t M, int N, int K, int sms) {
+  int best = 16;
+  double best_cost = 1e300;
+  for (int bn : {16, 32, 64}) {
+    if (N % bn) continue;
+    const double tiles = double(N / bn);
+    const double waves = double(int64_t((tiles + sms - 1) / sms));
+    const double cost = waves * (double(bn) + double((M + 7) / 8 * 8)) * double(K);
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+gdc_status launch_linear_skinny(const __half* a, int64_t lda, const __half* w, const __half* bias, __half* out,
+                                int64_t ldo, int64_t M, int N, int K, int act, cudaStream_t stream, int* err,
+                                const int32_t* m_dev) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int bn = choose_skinny_bn(M, N, K, device_sm_count(dev));
+  const int box_rows = int((M + 7) / 8 * 8);
+  CUtensorMap ta, tw;
+  GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), uint32_t(box_rows)));
+  GDC_TRY(make_tmap_2d(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn)));
+  const int m = int(M);
+#define GDC_SKINNY_CASE(BNV)                                                                                      \
+  if (bn == BNV) {                                                                                                \
+    if (act == kActGelu)                                                                                          \
+      return launch_skinny_variant<BNV, kActGelu>(ta, tw, bias, out, ldo, m, N, K, box_rows, stream, err, m_dev); \
+    if (act == kActRelu)                                                                                          \
+      return launch_skinny_variant<BNV, kActRelu>(ta, tw, bias, out, ldo, m, N, K, box_rows, stream, err, m_dev); \
+    return launch_skinny_variant<BNV, kActNone>(ta, tw, bias, out, ldo, m, N, K, box_rows, stream, err, m_dev);   \
+  }
+  GDC_SKINNY_CASE(16)
+  GDC_SKINNY_CASE(32)
+  GDC_SKINNY_CASE(64)
+#undef GDC_SKINNY_CASE
+  return set_error(GDC_ERR_UNSUPPORTED, "linear: no skinny tile for N=%d", N);
+}
+
 }  // namespace
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
@@ -353,14 +568,15 @@ gdc_status launch_linear(const __half* a, int64_t lda, const __half* w, const __
       (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(bias) & 15))
     return set_error(GDC_ERR_INVALID_INPUT, "linear: pointers must be 16-byte aligned and strides multiples of 8");
   if (act < 0 || act > 2) return set_error(GDC_ERR_INVALID_INPUT, "linear: unknown activation %d", act);
-  // Large M runs on CTA pairs (gemm_pair.cu); GDC_GEMM_SINGLE_CTA=1 selects this kernel for
-  // every M (used by tests to cross-check the two implementations).
+  // Large M runs on CTA pairs (gemm_pair.cu), M <= 128 on the skinny kernel; GDC_GEMM_SINGLE_CTA=1
+  // selects the persistent single-CTA kernel for every M (a cross-check of the implementations).
   static const bool force_single = [] {
     const char* e = std::getenv("GDC_GEMM_SINGLE_CTA");
     return e != nullptr && e[0] == '1';
   }();
   if (M > 128 && !force_single)
     return launch_linear_pair(a, lda, w, bias, out, ldo, M, N, K, act, stream, err, m_dev);
+  if (!force_single) return launch_linear_skinny(a, lda, w, bias, out, ldo, M, N, K, act, stream, err, m_dev);
   const int bn = (N % 256 == 0) ? 256 : 128;
   CUtensorMap ta, tw;
   GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), kBM));
