@@ -65,19 +65,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// A wait that has lasted this long starts checking the device error word: another thread of
+// the grid may have flagged a timeout, and then this wait gives up too instead of running to
+// its own limit. Shorter waits never read the (global) error word, so a wait that completes
+// normally is not held up by an outstanding global load when its phase flips.
+constexpr unsigned long long kErrCheckNs = 1000000ull;  // 1 ms
+
 // Waits until the phase with `parity` has completed. Returns false (and flags
 // kErrTimeoutBit in *err) if it does not within kTimeoutNs, or if another thread
-// of the grid has already flagged a timeout.
+// of the grid has already flagged a timeout (seen after kErrCheckNs of waiting).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
-      if (*reinterpret_cast<volatile int*>(err) & kErrTimeoutBit) return false;
-      if (globaltimer() - t0 > kTimeoutNs) {
-        atomicOr(err, kErrTimeoutBit);
-        return false;
+      const unsigned long long dt = globaltimer() - t0;
+      if (dt > kErrCheckNs) {
+        if (*reinterpret_cast<volatile int*>(err) & kErrTimeoutBit) return false;
+        if (dt > kTimeoutNs) {
+          atomicOr(err, kErrTimeoutBit);
+          return false;
+        }
       }
     }
   }
@@ -103,10 +112,13 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
   const unsigned long long t0 = globaltimer();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
-    if (*reinterpret_cast<volatile int*>(err) & kErrTimeoutBit) return false;
-    if (globaltimer() - t0 > kTimeoutNs) {
-      atomicOr(err, kErrTimeoutBit);
-      return false;
+    const unsigned long long dt = globaltimer() - t0;
+    if (dt > kErrCheckNs) {
+      if (*reinterpret_cast<volatile int*>(err) & kErrTimeoutBit) return false;
+      if (dt > kTimeoutNs) {
+        atomicOr(err, kErrTimeoutBit);
+        return false;
+      }
     }
   }
 }

@@ -82,6 +82,38 @@ def test_linear_matches_numpy(M, N, K, act):
     np.testing.assert_allclose(got, ref, rtol=2e-3, atol=2e-3)
 
 
+@pytest.mark.parametrize("M,N,K,act", [
+    (1, 4096, 1024, 1), (5, 3072, 1024, 0), (32, 3072, 1024, 0), (32, 1024, 1024, 0), (32, 1024, 4096, 0),
+    (32, 4096, 1024, 1), (96, 1024, 4096, 0), (128, 2048, 1024, 2), (7, 1024, 192, 0)])
+def test_linear_small_m_matches_numpy(M, N, K, act):
+    """M <= 128 (a batch of one short row; BASELINE config 0's projections have M = 32): the
+    skinny kernel, one narrow column tile per CTA over all of K, against float64 numpy; two
+    calls in a row give the same bits."""
+    torch = _torch()
+    rng = np.random.Generator(np.random.PCG64(M * 13 + N + K + act))
+    a = (rng.standard_normal((M, K), dtype=np.float32) * 0.5).astype(np.float16)
+    w = (rng.standard_normal((N, K), dtype=np.float32) / math.sqrt(K)).astype(np.float16)
+    b = (rng.standard_normal(N, dtype=np.float32) * 0.1).astype(np.float16)
+    da, dw, db = _dev(a), _dev(w), _dev(b)
+    ref = a.astype(np.float64) @ w.astype(np.float64).T + b.astype(np.float64)
+    if act == 1:
+        from scipy.special import erf
+        ref = 0.5 * ref * (1 + erf(ref / math.sqrt(2)))
+    elif act == 2:
+        ref = np.maximum(ref, 0)
+    outs = []
+    for _ in range(2):
+        out = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        _check(_lib().gdc_linear(da.data_ptr(), dw.data_ptr(), db.data_ptr(), out.data_ptr(), M, N, K, N, act, None))
+        torch.cuda.synchronize()
+        _check(_lib().gdc_kernels_check_errors())
+        got = _host(out)
+        assert np.isfinite(got.astype(np.float32)).all()
+        np.testing.assert_allclose(got.astype(np.float64), ref, rtol=2e-3, atol=2e-3)
+        outs.append(got)
+    assert np.array_equal(outs[0].view(np.uint16), outs[1].view(np.uint16))  # deterministic reduction
+
+
 def test_linear_leading_dimension():
     """Output written with ldo > N (the QKV projection writes into a wider buffer)."""
     torch = _torch()
