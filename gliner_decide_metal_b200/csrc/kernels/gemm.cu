@@ -291,38 +291,61 @@ gdc_status launch_gemm_variant(const CUtensorMap& ta, const CUtensorMap& tw, con
 // persistent CTA per 256-column tile (the kernel above) leaves most SMs idle, each of the
 // few busy ones streaming megabytes alone. Here every CTA owns one narrow column tile
 // (BN = 16, 32 or 64 columns) over all of K, so 64-148 CTAs stream the weights at once:
-//   warp 0 lane 0  TMA: per 128-column K block, the A rows [round_up(M, 8) x 128] (rows past
-//                  that stay stale in shared memory: the MMA rows they feed are not stored)
-//                  and the W tile [BN x 128], into an S-deep ring;
-//   warp 1 lane 0  tcgen05.mma M=128, N=BN, K=16 (8 per K block) into one TMEM accumulator;
+//   warp 0 lane 0  TMA: per 256-column K block, the A rows [round_up(M, 8) x 256] and the W
+//                  tile [BN x 256], one box each (four 64-column atoms back to back), into a
+//                  ring of up to 8 stages. A TMA box costs about the same whatever its size
+//                  up to 32 KB, so few, large boxes stream the weights fastest. The MMA reads
+//                  128 rows from each A atom: rows past round_up(M, 8) are whatever follows in
+//                  shared memory, and the MMA rows they feed are not stored;
+//   warp 1 lane 0  tcgen05.mma M=128, N=BN, K=16 (16 per K block) into one TMEM accumulator;
 //   warps 0-3      epilogue: TMEM lane quarter w, rows 32w..32w+31 below M: bias, GELU / ReLU,
 //                  fp16, 16-byte stores.
 // Each output element is one accumulation chain over K in order, as in the kernels above.
-constexpr int kSkBK = 128;
+constexpr int kSkBK = 256;
+constexpr int kSkAtoms = kSkBK / 64;
 constexpr int kSkThreads = 128;
+constexpr int kSkMaxStages = 8;
+constexpr int kSkRingBytes = 200 * 1024;
+constexpr int kSkSmemBytes = kSkRingBytes + 1024 + 256;
+
+// Ring layout for `box_rows` rows of A (a multiple of 8): per stage the A atoms box_rows x
+// 128 bytes apart, then room for the last atom's 128-row MMA read, then the W atoms.
+struct SkinnyRing {
+  int a_atom, a_bytes, stage_bytes, stages;
+};
+inline SkinnyRing skinny_ring(int box_rows, int bn) {
+  SkinnyRing r;
+  r.a_atom = box_rows * 128;
+  r.a_bytes = (kSkAtoms - 1) * r.a_atom + 128 * 128;
+  r.stage_bytes = r.a_bytes + kSkAtoms * bn * 128;
+  r.stages = kSkRingBytes / r.stage_bytes;
+  if (r.stages > kSkMaxStages) r.stages = kSkMaxStages;
+  return r;
+}
 
 template <int BN>
 struct SkinnyShape {
-  static constexpr int kAAtom = 128 * 64 * 2;  // 128 MMA rows x 64 K, 128-byte swizzle
   static constexpr int kBAtom = BN * 64 * 2;
-  static constexpr int kStageBytes = 2 * kAAtom + 2 * kBAtom;
-  static constexpr int kStages = (200 * 1024) / kStageBytes < 8 ? (200 * 1024) / kStageBytes : 8;
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
 };
 
 template <int BN, int ACT>
 __global__ void __launch_bounds__(kSkThreads, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                        const __half* __restrict__ bias, __half* __restrict__ out, int M_cap, int K, long long ldo,
-                       int a_box_rows, int* err, const int32_t* __restrict__ m_dev) {
+                       SkinnyRing ring, int* err, const int32_t* __restrict__ m_dev) {
   using S = SkinnyShape<BN>;
+  if (threadIdx.x == 0) {
+    ptx::prefetch_tensor_map(&tm_a);
+    ptx::prefetch_tensor_map(&tm_w);
+  }
   const int M = m_dev != nullptr ? min(M_cap, *m_dev) : M_cap;  // rows stored
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
-  uint64_t* empty = full + S::kStages;
-  uint64_t* done = empty + S::kStages;
+  const int stages = ring.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSkRingBytes);
+  uint64_t* empty = full + kSkMaxStages;
+  uint64_t* done = empty + kSkMaxStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -330,7 +353,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   const int kblocks = (K + kSkBK - 1) / kSkBK;  // a last half block reads TMA zero fill
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S::kStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
     }
@@ -345,43 +368,39 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  auto stage_a = [&](int s) { return smem + s * S::kStageBytes; };
-  auto stage_b = [&](int s) { return smem + s * S::kStageBytes + 2 * S::kAAtom; };
+  auto stage_a = [&](int s) { return smem + s * ring.stage_bytes; };
+  auto stage_b = [&](int s) { return smem + s * ring.stage_bytes + ring.a_bytes; };
 
   bool ok = true;
   if (warp == 0 && lane == 0) {
-    ptx::prefetch_tensor_map(&tm_a);
-    ptx::prefetch_tensor_map(&tm_w);
-    const uint32_t tx = 2u * uint32_t(a_box_rows * 128 + S::kBAtom);
+    const uint32_t tx = uint32_t(kSkAtoms) * uint32_t(ring.a_atom + S::kBAtom);
     int issued = 0;
     for (int kb = 0; kb < kblocks && ok; ++kb) {
-      const int s = kb % S::kStages;
-      if (!(ok = ptx::mbar_wait(&empty[s], uint32_t(((kb / S::kStages) & 1) ^ 1), err))) break;
+      const int s = kb % stages;
+      if (!(ok = ptx::mbar_wait(&empty[s], uint32_t(((kb / stages) & 1) ^ 1), err))) break;
       ptx::mbar_arrive_expect_tx(&full[s], tx);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        ptx::tma_load_2d(stage_a(s) + h * S::kAAtom, &tm_a, kb * kSkBK + h * 64, 0, &full[s]);
-        ptx::tma_load_2d(stage_b(s) + h * S::kBAtom, &tm_w, kb * kSkBK + h * 64, n0, &full[s]);
-      }
+      ptx::tma_load_3d(stage_a(s), &tm_a, 0, 0, kb * kSkAtoms, &full[s]);
+      ptx::tma_load_3d(stage_b(s), &tm_w, 0, n0, kb * kSkAtoms, &full[s]);
       ++issued;
     }
     // loads still in flight land before the CTA can exit (bounded)
-    for (int j = issued - S::kStages < 0 ? 0 : issued - S::kStages; j < issued; ++j) {
+    for (int j = issued - stages < 0 ? 0 : issued - stages; j < issued; ++j) {
       const unsigned long long t0 = ptx::globaltimer();
-      while (!ptx::mbar_try_wait(&full[j % S::kStages], uint32_t((j / S::kStages) & 1)) &&
+      while (!ptx::mbar_try_wait(&full[j % stages], uint32_t((j / stages) & 1)) &&
              ptx::globaltimer() - t0 < ptx::kTimeoutNs) {
       }
     }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = ptx::idesc_f16_f32(128, BN);
     for (int kb = 0; kb < kblocks; ++kb) {
-      const int s = kb % S::kStages;
-      if (!(ok = ptx::mbar_wait(&full[s], uint32_t((kb / S::kStages) & 1), err))) break;
+      const int s = kb % stages;
+      if (!(ok = ptx::mbar_wait(&full[s], uint32_t((kb / stages) & 1), err))) break;
       ptx::tc_fence_after();
       const uint32_t a_addr = ptx::smem_u32(stage_a(s)), b_addr = ptx::smem_u32(stage_b(s));
 #pragma unroll
       for (int k = 0; k < kSkBK / 16; ++k)
-        ptx::umma_f16_ss(tmem_base, ptx::desc_kmajor_sw128(a_addr + (k >> 2) * S::kAAtom + (k & 3) * 32),
+        ptx::umma_f16_ss(tmem_base,
+                         ptx::desc_kmajor_sw128(a_addr + uint32_t(k >> 2) * uint32_t(ring.a_atom) + (k & 3) * 32),
                          ptx::desc_kmajor_sw128(b_addr + (k >> 2) * S::kBAtom + (k & 3) * 32), idesc,
                          (kb | k) != 0 ? 1u : 0u);
       ptx::umma_commit(&empty[s]);
@@ -441,17 +460,17 @@ template <int BN, int ACT>
 gdc_status launch_skinny_variant(const CUtensorMap& ta, const CUtensorMap& tw, const __half* bias, __half* out,
                                  long long ldo, int M, int N, int K, int a_box_rows, cudaStream_t stream, int* err,
                                  const int32_t* m_dev) {
-  using S = SkinnyShape<BN>;
   auto kern = gemm_skinny_kernel<BN, ACT>;
   static PerDeviceOnce configured;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return set_error(GDC_ERR_CUDA, "device ordinal out of range");
   const cudaError_t ce = cudaError_t(per_device_once(configured, dev, [&] {
-    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSkSmemBytes);
   }));
   if (ce != cudaSuccess) return set_error(GDC_ERR_CUDA, "skinny gemm smem attribute: %s", cudaGetErrorString(ce));
-  kern<<<N / BN, kSkThreads, S::kSmemBytes, stream>>>(ta, tw, bias, out, M, K, ldo, a_box_rows, err, m_dev);
+  const SkinnyRing ring = skinny_ring(a_box_rows, BN);
+  kern<<<N / BN, kSkThreads, kSkSmemBytes, stream>>>(ta, tw, bias, out, M, K, ldo, ring, err, m_dev);
   return check_launch("gemm_skinny_kernel");
 }
 
@@ -481,8 +500,8 @@ gdc_status launch_linear_skinny(const __half* a, int64_t lda, const __half* w, c
   const int bn = choose_skinny_bn(M, N, K, device_sm_count(dev));
   const int box_rows = int((M + 7) / 8 * 8);
   CUtensorMap ta, tw;
-  GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), uint32_t(box_rows)));
-  GDC_TRY(make_tmap_2d(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn)));
+  GDC_TRY(make_tmap_katoms(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), uint32_t(box_rows), kSkAtoms));
+  GDC_TRY(make_tmap_katoms(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn), kSkAtoms));
   const int m = int(M);
 #define GDC_SKINNY_CASE(BNV)                                                                                      \
   if (bn == BNV) {                                                                                                \
@@ -529,6 +548,26 @@ gdc_status make_tmap_2d(void* map_out, const __half* base, uint64_t rows, uint64
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return GDC_OK;
+}
+
+gdc_status make_tmap_katoms(void* map_out, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                            uint32_t box_rows, uint32_t atoms) {
+  CUtensorMap* map = static_cast<CUtensorMap*>(map_out);
+  auto fn = get_encode_fn();
+  if (!fn) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (cols % 64 != 0) return set_error(GDC_ERR_UNSUPPORTED, "K-atom tensor map: %llu columns", (unsigned long long)cols);
+  // dimension order follows the shared-memory box (columns, rows, atoms); the atom stride
+  // (128 bytes) is below the row pitch, as in any tiled view whose modes are ordered by
+  // their shared-memory placement
+  cuuint64_t dims[3] = {64, rows, cols / 64};
+  cuuint64_t strides[2] = {ld * sizeof(__half), 64 * sizeof(__half)};
+  cuuint32_t box[3] = {64, box_rows, atoms};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(GDC_ERR_CUDA, "cuTensorMapEncodeTiled (K atoms) failed (%d)", int(r));
   return GDC_OK;
 }
 

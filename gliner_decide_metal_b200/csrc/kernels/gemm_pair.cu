@@ -45,7 +45,8 @@ struct PairShape {
   static constexpr int kStages = (200 * 1024) / kStageBytes;
   static constexpr int kTmemCols = (2 * BN <= 256) ? 256 : 512;
   static constexpr int kOutBytes = kEpiWarps * 2048;    // per epilogue warp: a 32 x 32 fp16 store box
-  static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 + 256;
+  static constexpr int kBiasBytes = kEpiWarps * 256;    // per epilogue warp: its <= 128 bias columns
+  static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kBiasBytes + 1024 + 256;
 };
 
 // erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26
@@ -103,30 +104,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                      const __half* __restrict__ bias, int M_cap, int N, int K, int* err,
                      const int32_t* __restrict__ m_dev) {
   using S = PairShape<BN>;
-  const int M = m_dev != nullptr ? min(M_cap, *m_dev) : M_cap;  // rows computed (same in both CTAs)
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // The descriptor fetches and the device row count's load are issued first, so their
+  // latency overlaps the barrier / TMEM set-up below instead of following it.
+  if (threadIdx.x == 0) {
+    ptx::prefetch_tensor_map(&tm_a);
+    ptx::prefetch_tensor_map(&tm_w);
+    ptx::prefetch_tensor_map(&tm_w_half);
+    ptx::prefetch_tensor_map(&tm_w_quarter);
+    ptx::prefetch_tensor_map(&tm_out);
+  }
+  const int m_read = m_dev != nullptr ? *m_dev : M_cap;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
   uint8_t* s_b = smem + S::kStages * S::kABytes;
   uint8_t* s_out = s_b + S::kStages * S::kBBytes;  // epilogue store boxes (1024-aligned)
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_out + S::kOutBytes);
+  uint8_t* s_bias = s_out + S::kOutBytes;          // epilogue bias columns
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_bias + S::kBiasBytes);
   uint64_t* empty = full + S::kStages;
   uint64_t* tfull = empty + S::kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
   const uint32_t rank = ptx::cluster_ctarank();
   const bool leader = rank == 0;
   const int kblocks = (K + kBK - 1) / kBK;  // a last half block reads TMA zero fill
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
-  // parts of BN keep the epilogue's 32-column chunks whole: BN = 256 splits in 2 or 4,
-  // BN = 128 in 2, BN = 192 not at all
-  const PairTiles tiles(M, N, BN, num_pairs, BN % 256 == 0 ? 4 : (BN % 128 == 0 ? 2 : 1));
-  const int num_tiles = tiles.num_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::kStages; ++s) {
@@ -149,13 +156,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   ptx::cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA signal
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const int M = min(M_cap, m_read);  // rows computed (same in both CTAs)
+  // parts of BN keep the epilogue's 32-column chunks whole: BN = 256 splits in 2 or 4,
+  // BN = 128 in 2, BN = 192 not at all
+  const PairTiles tiles(M, N, BN, num_pairs, BN % 256 == 0 ? 4 : (BN % 128 == 0 ? 2 : 1));
+  const int num_tiles = tiles.num_tiles;
 
   if (warp == 0) {
     if (lane == 0) {
-      ptx::prefetch_tensor_map(&tm_a);
-      ptx::prefetch_tensor_map(&tm_w);
-      ptx::prefetch_tensor_map(&tm_w_half);
-      ptx::prefetch_tensor_map(&tm_w_quarter);
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -172,13 +180,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           const uint32_t leader_full = ptx::mapa_shared(ptx::smem_u32(&full[stage]), 0);
           if (leader) ptx::mbar_arrive_expect_tx(&full[stage], tx);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            ptx::tma_load_2d_pair(s_a + stage * S::kABytes + h * S::kAHalf, &tm_a, kb * kBK + h * kAtomK,
-                                  ti.mb * 256 + int(rank) * 128, leader_full);
-            ptx::tma_load_2d_pair(s_b + stage * S::kBBytes + h * S::kBHalf, tw, kb * kBK + h * kAtomK,
-                                  ti.n0 + int(rank) * w_rows, leader_full);
-          }
+          // one box per operand: both 64-column atoms of the K block ([atom][row][64])
+          ptx::tma_load_3d_pair(s_a + stage * S::kABytes, &tm_a, 0, ti.mb * 256 + int(rank) * 128, kb * 2,
+                                leader_full);
+          ptx::tma_load_3d_pair(s_b + stage * S::kBBytes, tw, 0, ti.n0 + int(rank) * w_rows, kb * 2, leader_full);
           ++issued;
           if (++stage == S::kStages) {
             stage = 0;
@@ -221,6 +226,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
         const int tbn = tiles(tile).bn;
         const uint32_t idesc = tbn == BN ? idesc_full : (tbn == BN / 2 ? idesc_half : idesc_quarter);
+        const uint32_t b_atom = uint32_t(tbn) * 64;  // the W box's second atom: tbn / 2 rows of 128 bytes
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!ptx::mbar_wait(&full[stage], phase, err)) {
             ok = false;
@@ -232,7 +238,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint32_t off_a = uint32_t((k >> 2) * S::kAHalf + (k & 3) * 32);
-            const uint32_t off_b = uint32_t((k >> 2) * S::kBHalf + (k & 3) * 32);
+            const uint32_t off_b = uint32_t(k >> 2) * b_atom + uint32_t((k & 3) * 32);
             ptx::umma_f16_ss_pair(d_tmem, ptx::desc_kmajor_sw128(a_addr + off_a),
                                   ptx::desc_kmajor_sw128(b_addr + off_b), idesc, (kb | k) != 0 ? 1u : 0u);
           }
@@ -254,20 +260,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // Epilogue warps 2..(1 + kEpiWarps): TMEM lane quarter warp % 4, column half (warp-2)/4.
     // Each 32-row x 32-column chunk goes through this warp's 2 KB box in shared memory
     // (64-byte swizzle) and out with one TMA tensor store: full-line global writes instead
-    // of 16-byte stores to 32 different rows.
+    // of 16-byte stores to 32 different rows. The warp's bias columns of a tile are copied
+    // to shared memory before it waits for the accumulator, so their load latency hides
+    // behind the tile's main loop.
     const int quarter = warp & 3;
     const int col_half = (warp - 2) >> 2;
     uint8_t* box = s_out + (warp - 2) * 2048;
+    uint4* wbias = reinterpret_cast<uint4*>(s_bias + (warp - 2) * 256);
     uint8_t* box_row = box + lane * 64;
     const uint32_t box_swz = uint32_t((lane >> 1) & 3);
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
-      if (!ptx::mbar_wait(&tfull[acc], aphase, err)) break;
-      ptx::tc_fence_after();
       const PairTile ti = tiles(tile);
       const int half_cols = ti.bn / 2;  // columns of this warp's half of the tile
+      __syncwarp();                     // every lane is done reading the previous tile's bias
+      if (lane < half_cols / 8)
+        wbias[lane] = __ldg(reinterpret_cast<const uint4*>(bias + ti.n0 + col_half * half_cols) + lane);
+      __syncwarp();
+      if (!ptx::mbar_wait(&tfull[acc], aphase, err)) break;
+      ptx::tc_fence_after();
       const int row0 = ti.mb * 256 + int(rank) * 128 + quarter * 32;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
 #pragma unroll 1
@@ -277,11 +290,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ptx::tmem_ld_32x32b_x32(t_row + uint32_t(col), r);
         ptx::tmem_wait_ld();
         const int n0 = ti.n0 + col;
-        const uint4* bsrc = reinterpret_cast<const uint4*>(bias + n0);
         uint32_t packed[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint4 bv = __ldg(bsrc + q);
+          const uint4 bv = wbias[(c >> 3) + q];
           const __half2* bh = reinterpret_cast<const __half2*>(&bv);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -316,7 +328,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&tempty[acc]), 0));
     }
-    if (lane == 0) ptx::bulk_wait_group0();  // this warp's stores are complete before the CTA exits
+    // the stores have read this warp's box before the CTA exits (the grid's completion covers
+    // their global writes)
+    if (lane == 0) ptx::bulk_wait_group_read0();
   }
 
   ptx::tc_fence_before();
@@ -379,10 +393,10 @@ gdc_status launch_linear_pair(const __half* a, int64_t lda, const __half* w, con
   const int bn = (m_dev != nullptr && N % 256 == 0) ? 256 : choose_bn(M, N, device_sm_count(dev) / 2);
   if (bn == 0) return set_error(GDC_ERR_UNSUPPORTED, "linear: N=%d is not a multiple of 128", N);
   CUtensorMap ta, tw, twh, twq, to;
-  GDC_TRY(make_tmap_2d(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), 128));
-  GDC_TRY(make_tmap_2d(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 2)));
-  GDC_TRY(make_tmap_2d(&twh, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 4)));
-  GDC_TRY(make_tmap_2d(&twq, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 8 > 0 ? bn / 8 : 1)));
+  GDC_TRY(make_tmap_katoms(&ta, a, uint64_t(M), uint64_t(K), uint64_t(lda), 128, 2));
+  GDC_TRY(make_tmap_katoms(&tw, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 2), 2));
+  GDC_TRY(make_tmap_katoms(&twh, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 4), 2));
+  GDC_TRY(make_tmap_katoms(&twq, w, uint64_t(N), uint64_t(K), uint64_t(K), uint32_t(bn / 8 > 0 ? bn / 8 : 1), 2));
   GDC_TRY(make_tmap_2d_out32(&to, out, uint64_t(M), uint64_t(N), uint64_t(ldo)));
   const int m = int(M);
 #define GDC_PAIR_CASE(BNV)                                                                              \

@@ -113,6 +113,15 @@ gdc_status launch_wait_timeout_probe(int* err, int limit_us, cudaStream_t stream
 gdc_status make_tmap_2d(void* map, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld,
                         uint32_t box_rows);
 
+// K-atom fp16 TMA descriptor of a row-major `rows` x `cols` matrix (cols a multiple of 64,
+// row pitch `ld` elements): dimensions {64 columns, rows, cols / 64 atoms} with strides
+// {ld, 64 columns}, box {64, box_rows, atoms}, 128-byte swizzle. One load at {0, row, a}
+// writes `atoms` swizzle atoms of box_rows x 64 columns each back to back in shared
+// memory ([atom][row][64], atoms box_rows * 128 bytes apart): the K-major layout the MMA
+// reads, in one box instead of one per atom. Out-of-range rows and atoms read as zero.
+gdc_status make_tmap_katoms(void* map, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                            uint32_t box_rows, uint32_t atoms);
+
 // 2-D fp16 TMA descriptor for 32 x 32 output boxes (64-byte rows, 64-byte swizzle), used by
 // the GEMM epilogue's tensor stores; rows / columns beyond the extent are not written.
 gdc_status make_tmap_2d_out32(void* map, const __half* base, uint64_t rows, uint64_t cols, uint64_t ld);

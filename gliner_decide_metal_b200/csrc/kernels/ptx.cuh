@@ -137,6 +137,15 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tensor_m
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tensor_map, int32_t x, int32_t y, int32_t z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(tensor_map)), "r"(x), "r"(y), "r"(z),
+        "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 2-D tiled bulk tensor store shared -> global (bulk-group completion). Rows and columns
 // outside the tensor map's extent are not written.
 __device__ __forceinline__ void tma_store_2d(const void* tensor_map, int32_t x, int32_t y, const void* smem_src) {
@@ -283,6 +292,16 @@ __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* ten
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
       ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(tensor_map)), "r"(x), "r"(y),
+        "r"(mbar_cluster_addr)
+      : "memory");
+}
+
+// 3-D forms for the K-atom tensor maps (make_tmap_katoms): coordinates {0, row, first atom}.
+__device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const void* tensor_map, int32_t x, int32_t y,
+                                                 int32_t z, uint32_t mbar_cluster_addr) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(tensor_map)), "r"(x), "r"(y), "r"(z),
         "r"(mbar_cluster_addr)
       : "memory");
 }
