@@ -23,6 +23,7 @@
 #include <mutex>
 
 #include "kernels.h"
+#include "gelu.cuh"
 #include "ptx.cuh"
 
 namespace gdc {
@@ -43,21 +44,6 @@ struct GemmShape {
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
 };
 
-// erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26
-// (|error| <= 1.5e-7): erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2),
-// t = 1 / (1 + p x), x >= 0; odd extension for x < 0. The error is far below the fp16
-// rounding of the GEMM output.
-__device__ __forceinline__ float erf_as7126(float x) {
-  const float ax = fabsf(x);
-  const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
-  float poly = fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t,
-                    0.254829592f) * t;
-  const float y = 1.0f - poly * __expf(-ax * ax);
-  return copysignf(y, x);
-}
-
-// Exact-erf GELU of MLXNN.gelu (DeBERTa.swift:421): 0.5 x (1 + erf(x / sqrt 2)).
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f)); }
 
 template <int BN, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -227,17 +213,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const __half2* bh = reinterpret_cast<const __half2*>(&bv);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const float2 bf = __half22float2(bh[j]);
-              float v0 = __uint_as_float(r[half][q * 8 + 2 * j]) + bf.x;
-              float v1 = __uint_as_float(r[half][q * 8 + 2 * j + 1]) + bf.y;
+              float2 v = __fadd2_rn(
+                  make_float2(__uint_as_float(r[half][q * 8 + 2 * j]), __uint_as_float(r[half][q * 8 + 2 * j + 1])),
+                  __half22float2(bh[j]));
               if (ACT == kActGelu) {
-                v0 = gelu_erf(v0);
-                v1 = gelu_erf(v1);
+                v = gelu_erf2(v);
               } else if (ACT == kActRelu) {
-                v0 = fmaxf(v0, 0.f);
-                v1 = fmaxf(v1, 0.f);
+                v = make_float2(fmaxf(v.x, 0.f), fmaxf(v.y, 0.f));
               }
-              packed[q * 4 + j] = ptx::pack_half2(v0, v1);
+              packed[q * 4 + j] = ptx::pack_half2(v.x, v.y);
             }
           }
           if (row < M) {
@@ -429,17 +413,14 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           const __half2* bh = reinterpret_cast<const __half2*>(&bv);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float2 bf = __half22float2(bh[j]);
-            float v0 = __uint_as_float(r[q * 8 + 2 * j]) + bf.x;
-            float v1 = __uint_as_float(r[q * 8 + 2 * j + 1]) + bf.y;
+            float2 v = __fadd2_rn(make_float2(__uint_as_float(r[q * 8 + 2 * j]), __uint_as_float(r[q * 8 + 2 * j + 1])),
+                                  __half22float2(bh[j]));
             if (ACT == kActGelu) {
-              v0 = gelu_erf(v0);
-              v1 = gelu_erf(v1);
+              v = gelu_erf2(v);
             } else if (ACT == kActRelu) {
-              v0 = fmaxf(v0, 0.f);
-              v1 = fmaxf(v1, 0.f);
+              v = make_float2(fmaxf(v.x, 0.f), fmaxf(v.y, 0.f));
             }
-            packed[q * 4 + j] = ptx::pack_half2(v0, v1);
+            packed[q * 4 + j] = ptx::pack_half2(v.x, v.y);
           }
         }
         uint4* dst = reinterpret_cast<uint4*>(out + (long long)row * ldo + n0 + c0);

@@ -22,6 +22,7 @@
 #include <cuda.h>
 
 #include "kernels.h"
+#include "gelu.cuh"
 #include "ptx.cuh"
 
 namespace gdc {
@@ -49,17 +50,6 @@ struct PairShape {
   static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kBiasBytes + 1024 + 256;
 };
 
-// erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26
-// (|error| <= 1.5e-7): erf(x) = 1 - (a1 t + ... + a5 t^5) exp(-x^2), t = 1 / (1 + p x).
-__device__ __forceinline__ float erf_as7126(float x) {
-  const float ax = fabsf(x);
-  const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
-  const float poly =
-      fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t, 0.254829592f) * t;
-  return copysignf(1.0f - poly * __expf(-ax * ax), x);
-}
-
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f)); }
 
 // One output tile: 256-row block mb, columns [n0, n0 + bn).
 struct PairTile {
@@ -297,17 +287,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const __half2* bh = reinterpret_cast<const __half2*>(&bv);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float2 bf = __half22float2(bh[j]);
-            float v0 = __uint_as_float(r[q * 8 + 2 * j]) + bf.x;
-            float v1 = __uint_as_float(r[q * 8 + 2 * j + 1]) + bf.y;
+            float2 v = __fadd2_rn(make_float2(__uint_as_float(r[q * 8 + 2 * j]), __uint_as_float(r[q * 8 + 2 * j + 1])),
+                                  __half22float2(bh[j]));
             if (ACT == kActGelu) {
-              v0 = gelu_erf(v0);
-              v1 = gelu_erf(v1);
+              v = gelu_erf2(v);
             } else if (ACT == kActRelu) {
-              v0 = fmaxf(v0, 0.f);
-              v1 = fmaxf(v1, 0.f);
+              v = make_float2(fmaxf(v.x, 0.f), fmaxf(v.y, 0.f));
             }
-            packed[q * 4 + j] = ptx::pack_half2(v0, v1);
+            packed[q * 4 + j] = ptx::pack_half2(v.x, v.y);
           }
         }
         // the previous chunk's store has finished reading the box
