@@ -305,7 +305,7 @@ def kernel_classes(prof, steps, rows_timed, sum_ext2, sum_bl, markers_per_step, 
 
     for name, (n, k) in GEMMS.items():
         flops = 2.0 * n * k * rows_timed * LAYERS
-        byts = (2.0 * (rows_timed * (k + n)) + 2.0 * LAYERS * steps * (n * k + n))
+        byts = 2.0 * LAYERS * (rows_timed * (k + n) + steps * (n * k + n))
         out[name] = entry(name, flops, byts, "tensor")
     attn_flops = float(ATTN_FLOPS_PER_PAIR_LAYER) * sum_ext2 * LAYERS
     attn_bytes = LAYERS * (4.0 * rows_timed * HIDDEN * 2 + steps * POS_QK_BYTES + 2.0 * sum_bl)
