@@ -171,8 +171,8 @@ def _run_stream_tokens(models, examples: Sequence[TokenizedExample], buckets, ba
         rows_L.append(L)
     hm = max((len(ex.marker_positions) for ex in examples), default=1)
     o = max((len(m) for ex in examples for m in ex.marker_positions), default=1)
-    results: List[RawResult] = []
-    for start in range(0, len(examples), batch_size):
+
+    def prepare(start: int):
         chunk = examples[start:start + batch_size]
         t0 = time.perf_counter()
         B, L = len(chunk), max(rows_L[start:start + batch_size])
@@ -188,9 +188,37 @@ def _run_stream_tokens(models, examples: Sequence[TokenizedExample], buckets, ba
                 mi[r, h, :len(pos)] = pos
                 mm[r, h, :len(pos)] = 1
         prep_ms = (time.perf_counter() - t0) * 1e3 / B
-        logits, ms = _classify(models, DecisionInput(ids, mask, mi, mm))
-        for ex, preds in zip(chunk, _decode_chunk(logits, [ex.tasks for ex in chunk])):
-            results.append(RawResult(ex.id, preds, prep_ms, ms / B))
+        return chunk, DecisionInput(ids, mask, mi, mm), [prep_ms] * B
+
+    return _stream_pipeline(models, list(range(0, len(examples), batch_size)), prepare)
+
+
+def _stream_pipeline(models, keys: Sequence, prepare) -> List[RawResult]:
+    """The stream paths' chunk loop, pipelined: while chunk k is classified (in the C library,
+    without the interpreter lock) one worker thread prepares chunk k+1 (``prepare(key)`` ->
+    (rows, DecisionInput, per-row preprocessing ms)) and another decodes chunk k-1. Results
+    come back in input order."""
+    from concurrent.futures import ThreadPoolExecutor
+    results: List[RawResult] = []
+    if not keys:
+        return results
+
+    def finish(chunk, prep, logits, ms):
+        return [RawResult(ex.id, preds, p_ms, ms / len(chunk))
+                for ex, p_ms, preds in zip(chunk, prep, _decode_chunk(logits, [ex.tasks for ex in chunk]))]
+
+    with ThreadPoolExecutor(max_workers=2) as pool:
+        nxt = pool.submit(prepare, keys[0])
+        done = None
+        for k in range(len(keys)):
+            chunk, inp, prep = nxt.result()
+            if k + 1 < len(keys):
+                nxt = pool.submit(prepare, keys[k + 1])
+            logits, ms = _classify(models, inp)
+            if done is not None:
+                results.extend(done.result())
+            done = pool.submit(finish, chunk, prep, logits, ms)
+        results.extend(done.result())
     return results
 
 
@@ -227,15 +255,15 @@ def run_raw_examples(models, tokenizer, examples: Sequence[RawExample], buckets=
 
 
 def _run_stream_raw(models, tokenizer, examples: Sequence[RawExample], buckets, batch_size: int) -> List[RawResult]:
-    """``group_by="stream"`` from raw text, pipelined: a worker thread tokenises chunk k+1
-    while chunk k is classified (the classify call runs in the C library without the
-    interpreter lock). The marker arrays' width comes from the tasks (tasks per row, labels
-    per task), so every chunk has the same marker shape without tokenising ahead."""
-    from concurrent.futures import ThreadPoolExecutor
+    """``group_by="stream"`` from raw text, pipelined (``_stream_pipeline``): chunk k+1 is
+    tokenised and chunk k-1 decoded while chunk k is classified. The marker arrays' width
+    comes from the tasks (tasks per row, labels per task), so every chunk has the same marker
+    shape without tokenising ahead."""
     hm = max((len(ex.tasks) for ex in examples), default=1)
     o = max((len(t.labels) for ex in examples for t in ex.tasks), default=1)
 
-    def prepare(chunk: Sequence[RawExample]):
+    def prepare(start: int):
+        chunk = examples[start:start + batch_size]
         inputs, prep = [], []
         for ex in chunk:
             t0 = time.perf_counter()
@@ -243,22 +271,9 @@ def _run_stream_raw(models, tokenizer, examples: Sequence[RawExample], buckets, 
             prep.append((time.perf_counter() - t0) * 1e3)
         L = max(inp.shape[1] for inp in inputs)
         rows = [_pad_length(_pad_markers(inp, max(hm, inp.shape[2]), max(o, inp.shape[3])), L) for inp in inputs]
-        return DecisionInput.concatenated(rows), prep
+        return chunk, DecisionInput.concatenated(rows), prep
 
-    chunks = [examples[i:i + batch_size] for i in range(0, len(examples), batch_size)]
-    results: List[RawResult] = []
-    if not chunks:
-        return results
-    with ThreadPoolExecutor(max_workers=1) as pool:
-        nxt = pool.submit(prepare, chunks[0])
-        for k, chunk in enumerate(chunks):
-            inp, prep = nxt.result()
-            if k + 1 < len(chunks):
-                nxt = pool.submit(prepare, chunks[k + 1])
-            logits, ms = _classify(models, inp)
-            for ex, p_ms, preds in zip(chunk, prep, _decode_chunk(logits, [ex.tasks for ex in chunk])):
-                results.append(RawResult(ex.id, preds, p_ms, ms / len(chunk)))
-    return results
+    return _stream_pipeline(models, list(range(0, len(examples), batch_size)), prepare)
 
 
 def _pad_markers(inp: DecisionInput, hm: int, o: int) -> DecisionInput:
