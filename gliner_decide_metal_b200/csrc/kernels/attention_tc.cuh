@@ -73,6 +73,11 @@ constexpr int kCBWarpBytes = 32 * kCBPitch;
 // 16-byte drain stores; the reads of one row are contiguous).
 constexpr int kPBCols = 160;
 constexpr int kPBPitch = 336;
+// Context staging at an item's end, per row warp inside the P band: 32 rows x 64 bytes, rows
+// 80 bytes apart (5 chunks of 16 B: conflict-free 16-byte stores of 8 consecutive rows).
+constexpr int kStagePitch = 80;
+constexpr int kStageWarpBytes = 32 * kStagePitch;
+static_assert(kRowWarps * kStageWarpBytes <= 128 * kPBPitch, "context staging exceeds the P band");
 
 // shared memory map (offsets from the 1024-aligned base)
 constexpr int kOffQ = 0;                                 // Q tiles, 2 x 16 KB
@@ -567,7 +572,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tmask = s_tmask[slot];
       const bool has_valid = s_hasv[slot] != 0;
       const Item it = decode_item(item, n_kt, heads);
-      const int q = it.qt * kTile + t;
       const long long orow0 = s_row[slot];  // qkv / ctx row of position 0
       const int ext = s_ext[slot];
       float m_run = -INFINITY, l_part = 0.f;
@@ -722,12 +726,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      if (q < ext) {
+      {
         float lsum = s_red_l[t];
 #pragma unroll
         for (int pp = 1; pp < kParts; ++pp) lsum += s_red_l[pp * 128 + t];
-        const float inv = 1.0f / lsum;
-        __half* dst = ctx + (orow0 + q) * (long long)E + it.h * 64 + part * kOPP;
+        const float inv = 1.0f / lsum;  // rows past the extent are staged but never stored
+        // Stage the warp's 32 rows x 32 columns (64 bytes a row) in its slice of the P band,
+        // then store whole 64-byte row segments: 16 full sectors per store instruction instead
+        // of 32 half-filled ones (one row per lane). The slice is free: every row warp has
+        // read the P band of this item's last pair, and the next P drain into it follows the
+        // next pair's C drain of every row warp, which follows these stores.
+        uint8_t* stg = pband + warp * kStageWarpBytes;
 #pragma unroll
         for (int c = 0; c < kOPP / 8; ++c) {
           uint4 v;
@@ -735,7 +744,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           v.y = ptx::pack_half2(o[c * 8 + 2] * inv, o[c * 8 + 3] * inv);
           v.z = ptx::pack_half2(o[c * 8 + 4] * inv, o[c * 8 + 5] * inv);
           v.w = ptx::pack_half2(o[c * 8 + 6] * inv, o[c * 8 + 7] * inv);
-          reinterpret_cast<uint4*>(dst)[c] = v;
+          *reinterpret_cast<uint4*>(stg + lane * kStagePitch + 16 * c) = v;
+        }
+        __syncwarp();
+        __half* dst0 = ctx + it.h * 64 + part * kOPP + 8 * (lane & 3);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int r = 8 * j + (lane >> 2);  // row of this warp's 32
+          const int qr = it.qt * kTile + t0 + r;
+          const uint4 v = *reinterpret_cast<const uint4*>(stg + r * kStagePitch + 16 * (lane & 3));
+          if (qr < ext) *reinterpret_cast<uint4*>(dst0 + (orow0 + qr) * (long long)E) = v;
         }
       }
     }
