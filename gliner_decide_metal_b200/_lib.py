@@ -45,7 +45,7 @@ class GdcProfileEvent(C.Structure):
 
 
 class GdcOutput(C.Structure):
-    _fields_ = [("logits", C.POINTER(C.c_float)), ("logits_f16", C.POINTER(C.c_uint16)), ("wall_ns", C.c_uint64),
+    _fields_ = [("logits", C.c_void_p), ("logits_f16", C.c_void_p), ("wall_ns", C.c_uint64),
                 ("events", C.POINTER(GdcProfileEvent)), ("events_capacity", C.c_int32),
                 ("events_count", C.c_int32)]
 

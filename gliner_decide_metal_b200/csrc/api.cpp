@@ -107,6 +107,63 @@ gdc_status check_input_shape(const gdc_input* in) {
 
 // Converts a host gdc_input into the device staging layout (int32 ids, fp16 mask,
 // int32 markers, fp32 marker mask rounded through fp16 as the reference compares it).
+// Copies n integer ids of type S into dst as int32 and reports whether all lie in [0, hi).
+template <typename S>
+bool copy_ids_in_range(const void* src, int64_t n, int64_t hi, int32_t* dst) {
+  const S* s = static_cast<const S*>(src);
+  bool ok = true;
+  for (int64_t i = 0; i < n; ++i) {
+    const S v = s[i];
+    ok &= v >= 0 && int64_t(v) < hi;
+    dst[i] = int32_t(v);
+  }
+  return ok;
+}
+
+// Typed staging for the common dtypes: int32 / int64 ids and markers are range-checked and
+// narrowed in one pass, an fp16 mask is copied as is (fp16 -> float -> fp16 is the identity)
+// and a u8 mask goes through a 256-entry fp16 table; marker-mask values 0 and 1 are exact in
+// fp16. Returns false (nothing reported) when a value is out of range or a dtype has no fast
+// path; the element-wise pass below then stages the input and names the first bad value.
+bool stage_input_fast(gdc_model* m, const gdc_input* in, int64_t T, int64_t R, int32_t* ids, uint16_t* mask,
+                      int32_t* mk, float* mm) {
+  bool ok;
+  if (in->ids_dtype == GDC_INT32)
+    ok = copy_ids_in_range<int32_t>(in->input_ids, T, m->vocab, ids);
+  else if (in->ids_dtype == GDC_INT64)
+    ok = copy_ids_in_range<int64_t>(in->input_ids, T, m->vocab, ids);
+  else
+    return false;
+  if (!ok) return false;
+  if (in->marker_dtype == GDC_INT32)
+    ok = copy_ids_in_range<int32_t>(in->marker_indices, R, in->seq_len, mk);
+  else if (in->marker_dtype == GDC_INT64)
+    ok = copy_ids_in_range<int64_t>(in->marker_indices, R, in->seq_len, mk);
+  else
+    return false;
+  if (!ok) return false;
+  if (in->mask_dtype == GDC_FLOAT16) {
+    std::memcpy(mask, in->attention_mask, size_t(T) * 2);
+  } else if (in->mask_dtype == GDC_UINT8) {
+    static const std::vector<uint16_t> table = [] {
+      std::vector<uint16_t> t(256);
+      for (int v = 0; v < 256; ++v) t[size_t(v)] = __half_as_ushort(__float2half_rn(float(v)));
+      return t;
+    }();
+    const uint8_t* s = static_cast<const uint8_t*>(in->attention_mask);
+    for (int64_t i = 0; i < T; ++i) mask[i] = table[s[i]];
+  } else {
+    return false;
+  }
+  if (in->marker_mask_dtype != GDC_FLOAT32) return false;
+  const float* s = static_cast<const float*>(in->marker_mask);
+  for (int64_t i = 0; i < R; ++i) {
+    const float v = s[i];
+    mm[i] = (v == 0.f || v == 1.f) ? v : __half2float(__float2half_rn(v));
+  }
+  return true;
+}
+
 gdc_status stage_input(gdc_model* m, const gdc_input* in, uint8_t* dst) {
   const int64_t T = int64_t(in->batch) * in->seq_len;
   const int64_t R = int64_t(in->batch) * in->max_heads * in->max_options;
@@ -114,6 +171,7 @@ gdc_status stage_input(gdc_model* m, const gdc_input* in, uint8_t* dst) {
   uint16_t* mask = reinterpret_cast<uint16_t*>(dst + T * 4);
   int32_t* mk = reinterpret_cast<int32_t*>(dst + T * 6);
   float* mm = reinterpret_cast<float*>(dst + T * 6 + R * 4);
+  if (stage_input_fast(m, in, T, R, ids, mask, mk, mm)) return GDC_OK;
   for (int64_t i = 0; i < T; ++i) {
     int64_t v = 0;
     read_int(in->input_ids, in->ids_dtype, i, &v);
@@ -241,7 +299,12 @@ gdc_status gdc_classify(gdc_model* m, const gdc_input* in, int collect_profile, 
   if (st != GDC_OK) return st;
   GDC_CUDA_TRY(cudaMemcpyAsync(w.h_out, w.logits, size_t(R) * 4, cudaMemcpyDeviceToHost, s));
   GDC_CUDA_TRY(cudaMemcpyAsync(w.h_out + R * 4, w.logits16, size_t(R) * 2, cudaMemcpyDeviceToHost, s));
-  GDC_TRY(read_device_errors(m, s));  // synchronises
+  // the error word rides along into the pinned buffer (one synchronisation for both); a
+  // nonzero word is read again, cleared and reported by read_device_errors
+  const int* h_err = reinterpret_cast<const int*>(w.h_out + ((size_t(R) * 6 + 3) & ~size_t(3)));
+  GDC_CUDA_TRY(cudaMemcpyAsync(const_cast<int*>(h_err), m->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  GDC_CUDA_TRY(cudaStreamSynchronize(s));
+  if (*h_err != 0) GDC_TRY(read_device_errors(m, s));
   std::memcpy(out->logits, w.h_out, size_t(R) * 4);
   if (out->logits_f16) std::memcpy(out->logits_f16, w.h_out + R * 4, size_t(R) * 2);
   out->events_count = 0;

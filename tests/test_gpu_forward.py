@@ -118,6 +118,31 @@ def test_error_paths(weights_file):
     model.close()
 
 
+def test_input_dtypes_stage_identically(weights_file):
+    """Every supported host dtype of the four input arrays (typed staging for int32 / int64
+    ids and markers, fp16 / u8 masks, fp32 marker masks; element-wise staging for the rest)
+    gives the same logits bit for bit."""
+    import gliner_decide_metal_b200 as g
+    model, _ = _model(weights_file, 7, 2, 1000)
+    gld = load_golden("ragged_B3_L40_2L")
+    ids, mask, mi, mm = (gld[k] for k in ("input_ids", "attention_mask", "marker_indices", "marker_mask"))
+    base = model.classify(g.DecisionInput(ids.astype(np.int32), mask.astype(np.float16), mi.astype(np.int32),
+                                          mm.astype(np.float32))).logits_f32
+    for ids_t in (np.int32, np.int64):
+        for mask_t in (np.float16, np.float32, np.uint8, np.int32, np.int64):
+            for mi_t in (np.int32, np.int64):
+                for mm_t in (np.float32, np.float16, np.uint8):
+                    got = model.classify(g.DecisionInput(ids.astype(ids_t), mask.astype(mask_t), mi.astype(mi_t),
+                                                         mm.astype(mm_t))).logits_f32
+                    assert np.array_equal(got, base), (ids_t, mask_t, mi_t, mm_t)
+    # a bad id is still reported through the element-wise pass, with its position
+    bad = ids.astype(np.int32)
+    bad[1, 2] = 1000
+    with pytest.raises(g.InvalidInputError, match=r"input_ids\[\d+\] = 1000"):
+        model.classify(g.DecisionInput(bad, mask, mi, mm))
+    model.close()
+
+
 def test_profile_events_and_determinism(weights_file):
     import gliner_decide_metal_b200 as g
     model, _ = _model(weights_file, 7, 2, 1000)
