@@ -90,7 +90,7 @@ constexpr int kOffBits = kOffPB + 128 * kPBPitch;        // per item slot: 16 wo
 constexpr int kOffRed = kOffBits + 2 * 64;               // cross-part max exchange, kParts x 128 f32
 constexpr int kOffRedL = kOffRed + kParts * 512;         // cross-part denominator exchange
 constexpr int kOffFlags = kOffRedL + kParts * 512;       // per item slot: tile mask, item, extent, row base,
-                                                         // row-has-a-valid-key
+                                                         // row-has-a-valid-key, query tile | head
 constexpr int kOffBar = kOffFlags + 64;
 enum Bar {
   kBarFlags = 0, kBarQ0, kBarQ1, kBarQFree0, kBarQFree1, kBarKW, kBarWinFree, kBarV, kBarVFree, kBarC, kBarCDone,
@@ -242,6 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int32_t* s_ext = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 16);
   volatile int32_t* s_row = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 24);
   volatile int32_t* s_hasv = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 32);
+  volatile int32_t* s_qh = reinterpret_cast<volatile int32_t*>(sm + kOffFlags + 40);  // (query tile << 16) | head
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffTmemSlot);
 
@@ -368,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             s_ext[slot] = it_ext;
             s_row[slot] = it_row;
             s_hasv[slot] = has_valid ? 1 : 0;
+            s_qh[slot] = (it.qt << 16) | it.h;  // decoded once here, not by every row thread
             ptx::mbar_arrive(&bars[kBarFlags]);  // release: the item is visible to the consumers
             // Q buffer `slot` is free once the MMAs of item ni - 2 are done with it
             if (ni >= 2) ok = ptx::mbar_wait_sleep(&bars[kBarQFree0 + slot], uint32_t(((ni - 2) >> 1) & 1), err);
@@ -500,27 +502,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const bool has_next = nkt >= 0;
         const int qbuf = new_item ? ((ni + 1) & 1) : (ni & 1);
-        if (has_next) {
-          // C(np+1) as soon as P(np) has been drained and the next K / windows have landed:
-          // it runs while the rows score pair np
-          ok = ptx::mbar_wait(&bars[kBarKW], uint32_t((np + 1) & 1), err) &&
-               ptx::mbar_wait(&bars[kBarPDrained], par, err) &&
-               (!new_item || ptx::mbar_wait(&bars[kBarQ0 + qbuf], uint32_t(((ni + 1) >> 1) & 1), err));
-          if (!ok) break;
-          ptx::tc_fence_after();
-          issue_c(qbuf);
-        }
-        // PV(np): probabilities written to TMEM and O rescaled; the previous item's O read out
-        ok = ptx::mbar_wait(&bars[kBarProbs], par, err) && ptx::mbar_wait(&bars[kBarV], par, err) &&
-             (!first_in_item || ni == 0 || ptx::mbar_wait(&bars[kBarODone], uint32_t((ni - 1) & 1), err));
-        if (!ok) break;
-        ptx::tc_fence_after();
+        // C(np+1), looking ahead, as soon as P(np) has been drained and the next K / windows
+        // (and Q) have landed: it runs while the rows score pair np. PV(np) once the
+        // probabilities are in TMEM, O is rescaled and the previous item's O read out. The two
+        // touch different TMEM columns and operands, so whichever is ready is issued first:
+        // when the next loads land late, PV(np) does not queue behind C(np+1) in the tensor
+        // pipe (nor its completion behind C's). Every barrier polled here is at most one phase
+        // ahead of this thread, so the parity tests are exact.
+        bool c_todo = has_next, pv_todo = true;
+        ptx::PollLimit lim;
+        while (c_todo || pv_todo) {
+          if (c_todo && ptx::mbar_test_wait(&bars[kBarKW], uint32_t((np + 1) & 1)) &&
+              ptx::mbar_test_wait(&bars[kBarPDrained], par) &&
+              (!new_item || ptx::mbar_test_wait(&bars[kBarQ0 + qbuf], uint32_t(((ni + 1) >> 1) & 1)))) {
+            ptx::tc_fence_after();
+            issue_c(qbuf);
+            c_todo = false;
+          }
+          if (pv_todo && ptx::mbar_test_wait(&bars[kBarProbs], par) && ptx::mbar_test_wait(&bars[kBarV], par) &&
+              (!first_in_item || ni == 0 || ptx::mbar_test_wait(&bars[kBarODone], uint32_t((ni - 1) & 1)))) {
+            ptx::tc_fence_after();
 #pragma unroll
-        for (int s = 0; s < 8; ++s)
-          ptx::umma_f16_ts(tbase + kColO, tbase + kColProb + uint32_t(8 * s), ptx::desc_mnmajor_sw128(aV + s * 2048),
-                           id_pv, (s > 0 || !first_in_item) ? 1u : 0u);
-        ptx::umma_commit(&bars[kBarO]);
-        ptx::umma_commit(&bars[kBarVFree]);
+            for (int s = 0; s < 8; ++s)
+              ptx::umma_f16_ts(tbase + kColO, tbase + kColProb + uint32_t(8 * s),
+                               ptx::desc_mnmajor_sw128(aV + s * 2048), id_pv, (s > 0 || !first_in_item) ? 1u : 0u);
+            ptx::umma_commit(&bars[kBarO]);
+            ptx::umma_commit(&bars[kBarVFree]);
+            pv_todo = false;
+          }
+          if (!(ok = lim.ok(err))) break;
+          // a short pause between polls leaves the issue slots of this SM sub-partition to the
+          // row warps scoring the pair
+          if (c_todo || pv_todo) __nanosleep(32);
+        }
+        if (!ok) break;
         if (has_next) {
           // S(np+1): the rows have consumed S(np) (their probabilities are written)
           issue_s(qbuf);
@@ -571,7 +586,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (item < 0) break;
       const uint32_t tmask = s_tmask[slot];
       const bool has_valid = s_hasv[slot] != 0;
-      const Item it = decode_item(item, n_kt, heads);
+      const int qh = s_qh[slot];
+      const int it_qt = qh >> 16, it_h = qh & 0xffff;
       const long long orow0 = s_row[slot];  // qkv / ctx row of position 0
       const int ext = s_ext[slot];
       float m_run = -INFINITY, l_part = 0.f;
@@ -747,11 +763,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(stg + lane * kStagePitch + 16 * c) = v;
         }
         __syncwarp();
-        __half* dst0 = ctx + it.h * 64 + part * kOPP + 8 * (lane & 3);
+        __half* dst0 = ctx + it_h * 64 + part * kOPP + 8 * (lane & 3);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int r = 8 * j + (lane >> 2);  // row of this warp's 32
-          const int qr = it.qt * kTile + t0 + r;
+          const int qr = it_qt * kTile + t0 + r;
           const uint4 v = *reinterpret_cast<const uint4*>(stg + r * kStagePitch + 16 * (lane & 3));
           if (qr < ext) *reinterpret_cast<uint4*>(dst0 + (orow0 + qr) * (long long)E) = v;
         }

@@ -92,6 +92,40 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// Non-blocking test of a phase (test_wait never suspends the thread), for a thread that polls
+// several barriers and acts on whichever completes first.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Time limit of a polling loop, with the same rules as mbar_wait: gives up (false) once
+// another thread of the grid has flagged a timeout (checked after kErrCheckNs) or, flagging
+// kErrTimeoutBit itself, after kTimeoutNs.
+struct PollLimit {
+  unsigned long long t0;
+  uint32_t spins = 0;
+  __device__ __forceinline__ PollLimit() : t0(globaltimer()) {}
+  __device__ __forceinline__ bool ok(int* err) {
+    if ((++spins & 255u) != 0) return true;
+    const unsigned long long dt = globaltimer() - t0;
+    if (dt <= kErrCheckNs) return true;
+    if (*reinterpret_cast<volatile int*>(err) & kErrTimeoutBit) return false;
+    if (dt > kTimeoutNs) {
+      atomicOr(err, kErrTimeoutBit);
+      return false;
+    }
+    return true;
+  }
+};
+
 // try_wait that may suspend the thread for up to `hint_ns` (it resumes as soon as the
 // phase completes), so waiting warps give their issue slots to the warps doing work.
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
