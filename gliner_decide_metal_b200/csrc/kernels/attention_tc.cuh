@@ -32,7 +32,8 @@
 //         pair's P MMA has consumed them, V once the previous pair's PV has.
 //   MMA   per pair n:  P(n) = K PQw^T after the C drain; then, looking ahead, C(n+1) =
 //         Q PKw^T as soon as P(n) has been drained and the next windows landed (it runs while
-//         the rows score pair n); PV(n) once the probabilities are in TMEM; S(n+1) = Q K^T.
+//         the rows score pair n) and PV(n) once the probabilities are in TMEM, in whichever
+//         order their inputs become ready; then S(n+1) = Q K^T.
 //         TMEM: S cols 0-127, C / P cols 128-383, O cols 384-447, probabilities 448-511.
 //   rows  drain the C columns their own rows need (the band [t0+64-64p, +96) of 255) to
 //         shared memory, the P rows of their lane quarter over the columns any query row needs
