@@ -531,10 +531,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::umma_commit(&bars[kBarVFree]);
             pv_todo = false;
           }
+          // no pause between polls: measured against 32 and 100 ns pauses, the row warps
+          // sharing this SM sub-partition lost nothing to the spin and the issue came sooner
           if (!(ok = lim.ok(err))) break;
-          // a short pause between polls leaves the issue slots of this SM sub-partition to the
-          // row warps scoring the pair
-          if (c_todo || pv_todo) __nanosleep(32);
         }
         if (!ok) break;
         if (has_next) {
